@@ -1,0 +1,168 @@
+/*
+ * llm_b200.h -- the C ABI of the B200 forward pass for go-wasmcontainers/llm.
+ *
+ * A drop-in for the reference's GPU forward pass (gpu.go, fused.go,
+ * kernels.go, kernels_fused.go): a Go host keeps its llm.GPU API and calls
+ * these functions over cgo instead of recording WebGPU passes.  Each entry
+ * point names the reference interface it replaces (file:line in the
+ * reference repository).  Plain C types only; the library owns all device
+ * memory, the caller owns every buffer it passes in.  No call aborts the
+ * process: every failure is a status code with a message from
+ * llmb_last_error.
+ *
+ * Threading (gpu.go:148,831): a model handle is used by one thread at a
+ * time.  Several handles, one per device, may run concurrently from
+ * separate threads; that is the multi-GPU mode (independent sequences).
+ */
+#ifndef LLM_B200_H
+#define LLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define LLMB_API __attribute__((visibility("default")))
+#else
+#define LLMB_API
+#endif
+
+/* Status codes.  The reference returns Go error values; the classes below
+ * follow its error sites. */
+enum {
+    LLMB_OK = 0,
+    LLMB_ERR_ARG = 1,     /* a bad argument (empty prompt gpu.go:855, token id out of range) */
+    LLMB_ERR_IO = 2,      /* reading the model file (gpu.go:365-367) */
+    LLMB_ERR_FORMAT = 3,  /* GGUF header: gguf.ErrMagic, ErrVersion, ErrFormat (gguf/gguf.go:29-34) */
+    LLMB_ERR_BOUND = 4,   /* GGUF header: gguf.ErrBound (gguf/gguf.go:32) */
+    LLMB_ERR_CONFIG = 5,  /* ConfigFrom refusals (config.go:32-70) */
+    LLMB_ERR_TENSOR = 6,  /* a missing tensor or a type without a kernel (gpu.go:300,326) */
+    LLMB_ERR_MEMORY = 7,  /* the memory budget or a device allocation (gpu.go:175-177) */
+    LLMB_ERR_CONTEXT = 8, /* prompt and new tokens exceed the context (gpu.go:948-950, 905-907) */
+    LLMB_ERR_CUDA = 9,    /* a CUDA runtime error */
+    LLMB_ERR_DEVICE = 10  /* a kernel reported an error (a bounded wait that gave up) */
+};
+
+typedef struct llmb_model llmb_model;
+
+/* Config, config.go:11-23. */
+typedef struct {
+    int32_t layers, embd, ff, heads, kv_heads, head_dim, vocab, ctx;
+    float rope_base, eps;
+    int32_t rope_neox, bias, tied_output;
+    char arch[16];
+} llmb_config;
+
+/* Stats, gpu.go:55-60.  A submit is one host->device launch group (one
+ * CUDA graph launch or one prefill chunk); a dispatch is one kernel. */
+typedef struct {
+    int64_t submits, dispatches, tokens;
+} llmb_stats;
+
+/* Timing, gpu.go:929-939, plus device time from CUDA events on the model's
+ * stream.  prefill_ms runs until the first sampled token is on the host;
+ * decode_ms is the rest of the call.  gpu_decode_ms spans the first decode
+ * launch to the end of the last; decode_kernel_ms sums the decode launches
+ * alone (decode_launches of them). */
+typedef struct {
+    double prefill_ms, decode_ms;         /* wall clock, as time.Since in Generate */
+    int32_t prompt_tokens, generated;
+    int64_t submits, dispatches;
+    double record_ms, submit_ms;          /* host time launching / waiting in decode */
+    double gpu_prefill_ms, gpu_decode_ms; /* device time between CUDA events */
+    double decode_kernel_ms;
+    int64_t decode_launches;
+} llmb_timing;
+
+/* A reader of the model file: fill buf with len bytes at offset, return 0
+ * on success.  Lets a Go host pass its io.ReaderAt (gpu.go:290,365). */
+typedef int (*llmb_read_fn)(void *user, uint64_t offset, void *buf, uint64_t len);
+
+/* Called with each generated token in order; return nonzero to go on, 0 to
+ * stop (the emit callback of Generate, gpu.go:946,979). */
+typedef int (*llmb_emit_fn)(void *user, int32_t token);
+
+/* NewGPU, gpu.go:465-764.  Parses the GGUF header (gguf.Parse,
+ * gguf/gguf.go:292), checks the configuration (ConfigFrom, config.go:29),
+ * allocates every device buffer, builds the RoPE table in double precision
+ * (gpu.go:524-541) and streams the weights through pinned host buffers into
+ * their device layout.  ctx <= 0 or above the model's context_length means
+ * context_length (gpu.go:470-472).  device is the CUDA ordinal. */
+LLMB_API int llmb_open(const char *gguf_path, int ctx, int device, llmb_model **out);
+
+/* NewGPU over a reader callback instead of a path; size is the file size. */
+LLMB_API int llmb_open_reader(llmb_read_fn read, void *user, uint64_t size, int ctx, int device, llmb_model **out);
+
+/* Releases every device and host resource of the model. */
+LLMB_API void llmb_close(llmb_model *m);
+
+/* The message of the last failure on this model; with m == NULL, the last
+ * failure of llmb_open / llmb_open_reader on the calling thread.  Never NULL. */
+LLMB_API const char *llmb_last_error(const llmb_model *m);
+
+/* GPU.Cfg, gpu.go:119. */
+LLMB_API int llmb_get_config(const llmb_model *m, llmb_config *out);
+
+/* GPU.MemoryUsed, gpu.go:766-767: device bytes the model, its cache and its
+ * scratch hold. */
+LLMB_API uint64_t llmb_memory_used(const llmb_model *m);
+
+/* GPU.Stats, gpu.go:138. */
+LLMB_API int llmb_get_stats(const llmb_model *m, llmb_stats *out);
+
+/* Generate, gpu.go:941-1014: greedy decoding.  The prompt goes through the
+ * layers in chunks of up to PrefillBatch tokens, then tokens are decoded in
+ * launches of DecodeBatch tokens, each sampled on the GPU (first index of the
+ * largest logit) from the one before; only the sampled ids come back.
+ * Stops after n tokens, at eos (not emitted) or when emit returns 0.  The
+ * next launch is queued before the tokens of the one before are read back,
+ * so up to 2*DecodeBatch-1 tokens may have been computed past the stop
+ * (DecodeBatch-1 in the reference, gpu.go:1048-1051).  Each call starts at
+ * position 0.  emit may be NULL.
+ * out_tokens (may be NULL) receives the emitted tokens, n_out their count
+ * (may be NULL), tm the timing (may be NULL). */
+LLMB_API int llmb_generate(llmb_model *m, const int32_t *prompt, int n_prompt, int n, int32_t eos, llmb_emit_fn emit,
+                  void *user, int32_t *out_tokens, int *n_out, llmb_timing *tm);
+
+/* PrefillLogits, gpu.go:902-927: runs the prompt and copies the vocab
+ * logits of its last token into logits (a test hook: Generate never reads
+ * logits back). */
+LLMB_API int llmb_prefill_logits(llmb_model *m, const int32_t *prompt, int n_prompt, float *logits);
+
+/* A test hook with no single counterpart in the reference: the greedy run
+ * of Generate (prompt, then n tokens) that also copies the logits which
+ * chose each token into step_logits (n rows of vocab floats), so that a
+ * test checks every step against the CPU path, as examples/generate check
+ * (main.go:141-181) does for step 1.  Decodes one token per launch. */
+LLMB_API int llmb_generate_logits(llmb_model *m, const int32_t *prompt, int n_prompt, int n, int32_t *out_tokens,
+                         float *step_logits);
+
+/* Peek, gpu.go:1016-1043: the first n 32-bit words of a named device buffer,
+ * as floats.  Names: "x" (residual stream), "q", "att", "gate" (the SwiGLU
+ * output), "logits", "state" ({position, step} as raw bits), "tokens",
+ * and "kvblk.N." (layer N's cache: K then V). */
+LLMB_API int llmb_peek(llmb_model *m, const char *name, float *out, int n);
+
+/* GPU.Layers, gpu.go:143-146: run only that many layers (debugging: no
+ * logits and no sampling are then produced).  0 restores all layers. */
+LLMB_API int llmb_set_layers(llmb_model *m, int layers);
+
+/* The package knobs of the reference: "decode_batch" (DecodeBatch,
+ * gpu.go:1052, clamped to 1..16 as gpu.go:1046,1054), "prefill_batch"
+ * (PrefillBatch, gpu.go:165; read by llmb_open, 1..64) and "memory_budget"
+ * (Limits.MemoryBudget, gpu.go:35; bytes, 0 = the device's free memory;
+ * read by llmb_open).  One more, with no counterpart in the reference:
+ * "decode_mode" 0 (default) decodes with the persistent kernel, 1 with one
+ * kernel per phase (an A/B and debugging aid).  Process-wide, like the Go
+ * package variables. */
+LLMB_API int llmb_set_knob(const char *name, int64_t value);
+LLMB_API int64_t llmb_get_knob(const char *name);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLM_B200_H */

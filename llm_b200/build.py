@@ -1,0 +1,54 @@
+"""Builds llm_b200/libllmb200.so with nvcc for sm_100a (in-tree, so it travels with the repository).
+
+    python -m llm_b200.build          # incremental
+    python -m llm_b200.build --force  # rebuild everything
+"""
+
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libllmb200.so")
+SOURCES = ["gguf.cpp", "kernels.cu", "engine.cu"]
+HEADERS = ["gguf.hpp", "device.hpp", "kernels.hpp", os.path.join("..", "..", "include", "llm_b200.h")]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", os.path.join(ROOT, "include")]
+
+
+def _nvcc() -> str:
+    for c in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", "nvcc"):
+        if c and (os.path.isabs(c) and os.path.exists(c) or not os.path.isabs(c)):
+            return c
+    return "nvcc"
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    hdr_mtime = max(os.path.getmtime(os.path.join(CSRC, h)) for h in HEADERS)
+    objs, newest = [], 0.0
+    for src in SOURCES:
+        s = os.path.join(CSRC, src)
+        o = os.path.join(BUILD, src + ".o")
+        objs.append(o)
+        if force or not os.path.exists(o) or os.path.getmtime(o) < max(os.path.getmtime(s), hdr_mtime):
+            cmd = [_nvcc(), *ARCH, *FLAGS, "-c", s, "-o", o]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+            subprocess.run(cmd, check=True)
+        newest = max(newest, os.path.getmtime(o))
+    if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
+        tmp = LIB + ".tmp"
+        subprocess.run([_nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-lrt", "-ldl", "-lpthread"],
+                       check=True)
+        os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

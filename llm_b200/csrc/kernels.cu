@@ -1,0 +1,749 @@
+// Forward-pass kernels for sm_100a: batch-1 decode and chunked prefill of
+// llama / qwen2 models with Q4_0, Q4_1 and Q8_0 weights and an f32 KV cache.
+//
+// The math restates the reference's CPU f32 path (cpu.go:225-366) and its
+// fused WGSL kernels (kernels_fused.go:28-170, kernels.go:19-415); the
+// shapes are B200's, not WebGPU's:
+//   - a warp computes one tile of 8 output rows; lane (r, q) = (lane/4,
+//     lane%4) owns row r and 8 of each block's 32 weights, so every block of
+//     a tile is one 128- or 256-byte coalesced load and the 4 partial sums of
+//     a row meet in two shuffles;
+//   - nibbles become floats exactly with a byte permute into the mantissa of
+//     2^23 (no integer-to-float conversion);
+//   - RMSNorm is recomputed by every CTA that needs it (K1, K4 of
+//     kernels_fused.go), RoPE and the KV append are the epilogue of the QKV
+//     product, SwiGLU the epilogue of gate/up, the residual add the epilogue
+//     of the output and down products;
+//   - attention is split over chunks of 64 positions (flash-decoding, as K2
+//     of kernels_fused.go:75-146); the last CTA of a head to finish merges
+//     its chunks (K3's merge, kernels_fused.go:148-170), so the output
+//     projection reads a finished vector;
+//   - the vocab argmax (first index of the largest logit, cpu.go:387-397)
+//     is fused into the head product: per-CTA partials, then a final pass.
+// Every phase is a device function over work items, called from per-phase
+// kernels (m tokens) and from one persistent cooperative decode kernel that
+// separates the phases with bounded grid barriers.
+#include <cuda_fp16.h>
+
+#include <cfloat>
+#include <cstdint>
+
+#include "kernels.hpp"
+
+namespace llmb {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+// Block-wide reductions over kThreads threads; red holds >= kWarps floats.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    return warp_sum(l < kWarps ? red[l] : 0.f);
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    return warp_max(l < kWarps ? red[l] : -FLT_MAX);
+}
+
+// Byte k of v (0..255) plus 2^23, as a float: exact, one byte permute.
+__device__ __forceinline__ float b2f(uint32_t v, int k) {
+    return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | k));
+}
+
+// ---------------------------------------------------------------- dot --
+// Each returns, in all 4 lanes of row r = lane / 4, the dot product of tile
+// row r with the vector xs (shared memory, nb * 32 floats).
+
+// Q4_0: value d * (q - 8); byte j of a block holds element j (low nibble)
+// and j + 16 (high nibble) (cpu.go:164-179).  Lane q owns bytes 4q..4q+3.
+__device__ __forceinline__ float dot_q4_0(const uint8_t *__restrict__ tile, int nb, const float *__restrict__ xs,
+                                          int lane) {
+    const int r = lane >> 2, q = lane & 3;
+    const uint32_t *qw = reinterpret_cast<const uint32_t *>(tile) + r * 4 + q;
+    const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 128) + r;
+    const float *xp = xs + 4 * q;
+    constexpr float kOff = 8388616.f;  // 2^23 + 8
+    float acc = 0.f;
+#pragma unroll 2
+    for (int b = 0; b < nb; ++b) {
+        const uint32_t w = __ldg(qw + b * 32);
+        const float d = __half2float(__ldg(dp + b * 8));
+        const float4 x0 = *reinterpret_cast<const float4 *>(xp + b * 32);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xp + b * 32 + 16);
+        const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+        float s = (b2f(lo, 0) - kOff) * x0.x;
+        s = fmaf(b2f(hi, 0) - kOff, x1.x, s);
+        s = fmaf(b2f(lo, 1) - kOff, x0.y, s);
+        s = fmaf(b2f(hi, 1) - kOff, x1.y, s);
+        s = fmaf(b2f(lo, 2) - kOff, x0.z, s);
+        s = fmaf(b2f(hi, 2) - kOff, x1.z, s);
+        s = fmaf(b2f(lo, 3) - kOff, x0.w, s);
+        s = fmaf(b2f(hi, 3) - kOff, x1.w, s);
+        acc = fmaf(d, s, acc);
+    }
+    acc += __shfl_xor_sync(kFull, acc, 1);
+    acc += __shfl_xor_sync(kFull, acc, 2);
+    return acc;
+}
+
+// Q4_1: value d * q + m (cpu.go:181-200): sum d * sum(q x) + m * sum(x).
+__device__ __forceinline__ float dot_q4_1(const uint8_t *__restrict__ tile, int nb, const float *__restrict__ xs,
+                                          int lane) {
+    const int r = lane >> 2, q = lane & 3;
+    const uint32_t *qw = reinterpret_cast<const uint32_t *>(tile) + r * 4 + q;
+    const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 128) + r;
+    const __half *mp = dp + nb * 8;
+    const float *xp = xs + 4 * q;
+    constexpr float kOff = 8388608.f;  // 2^23
+    float acc = 0.f;
+#pragma unroll 2
+    for (int b = 0; b < nb; ++b) {
+        const uint32_t w = __ldg(qw + b * 32);
+        const float d = __half2float(__ldg(dp + b * 8));
+        const float mn = __half2float(__ldg(mp + b * 8));
+        const float4 x0 = *reinterpret_cast<const float4 *>(xp + b * 32);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xp + b * 32 + 16);
+        const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+        float s = (b2f(lo, 0) - kOff) * x0.x;
+        s = fmaf(b2f(hi, 0) - kOff, x1.x, s);
+        s = fmaf(b2f(lo, 1) - kOff, x0.y, s);
+        s = fmaf(b2f(hi, 1) - kOff, x1.y, s);
+        s = fmaf(b2f(lo, 2) - kOff, x0.z, s);
+        s = fmaf(b2f(hi, 2) - kOff, x1.z, s);
+        s = fmaf(b2f(lo, 3) - kOff, x0.w, s);
+        s = fmaf(b2f(hi, 3) - kOff, x1.w, s);
+        const float sx = ((x0.x + x0.y) + (x0.z + x0.w)) + ((x1.x + x1.y) + (x1.z + x1.w));
+        acc += fmaf(d, s, mn * sx);
+    }
+    acc += __shfl_xor_sync(kFull, acc, 1);
+    acc += __shfl_xor_sync(kFull, acc, 2);
+    return acc;
+}
+
+// Q8_0: value d * int8 (cpu.go:201-215).  Lane q owns bytes 8q..8q+7.
+__device__ __forceinline__ float dot_q8_0(const uint8_t *__restrict__ tile, int nb, const float *__restrict__ xs,
+                                          int lane) {
+    const int r = lane >> 2, q = lane & 3;
+    const uint2 *qw = reinterpret_cast<const uint2 *>(tile) + r * 4 + q;
+    const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 256) + r;
+    const float *xp = xs + 8 * q;
+    constexpr float kOff = 8388736.f;  // 2^23 + 128: bytes are biased by 128
+    float acc = 0.f;
+#pragma unroll 2
+    for (int b = 0; b < nb; ++b) {
+        const uint2 w = __ldg(qw + b * 32);
+        const float d = __half2float(__ldg(dp + b * 8));
+        const float4 x0 = *reinterpret_cast<const float4 *>(xp + b * 32);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xp + b * 32 + 4);
+        const uint32_t u0 = w.x ^ 0x80808080u, u1 = w.y ^ 0x80808080u;
+        float s = (b2f(u0, 0) - kOff) * x0.x;
+        s = fmaf(b2f(u0, 1) - kOff, x0.y, s);
+        s = fmaf(b2f(u0, 2) - kOff, x0.z, s);
+        s = fmaf(b2f(u0, 3) - kOff, x0.w, s);
+        s = fmaf(b2f(u1, 0) - kOff, x1.x, s);
+        s = fmaf(b2f(u1, 1) - kOff, x1.y, s);
+        s = fmaf(b2f(u1, 2) - kOff, x1.z, s);
+        s = fmaf(b2f(u1, 3) - kOff, x1.w, s);
+        acc = fmaf(d, s, acc);
+    }
+    acc += __shfl_xor_sync(kFull, acc, 1);
+    acc += __shfl_xor_sync(kFull, acc, 2);
+    return acc;
+}
+
+__device__ __forceinline__ float tile_dot(const QMat &m, int tile, const float *xs, int lane) {
+    const uint8_t *t = m.tiles + (size_t)tile * m.tile_bytes;
+    switch (m.type) {
+    case 3: return dot_q4_1(t, m.nb, xs, lane);
+    case 8: return dot_q8_0(t, m.nb, xs, lane);
+    default: return dot_q4_0(t, m.nb, xs, lane);
+    }
+}
+
+// Element e of row `row` of a tile-layout matrix, dequantised (the embedding
+// gather, kernels.go:19-73 / cpu.go:231-254).
+__device__ __forceinline__ float gather(const QMat &m, int row, int e) {
+    const uint8_t *t = m.tiles + (size_t)(row >> 3) * m.tile_bytes;
+    const int r = row & 7, b = e >> 5, j = e & 31;
+    const int qb = m.type == 8 ? 32 : 16;
+    const float d = __half2float(reinterpret_cast<const __half *>(t + (size_t)m.nb * 8 * qb)[b * 8 + r]);
+    const uint8_t *qs = t + ((size_t)b * 8 + r) * qb;
+    if (m.type == 8) return d * (float)(int8_t)qs[j];
+    const uint8_t byte = qs[j & 15];
+    const int nib = j < 16 ? (byte & 15) : (byte >> 4);
+    return d * (float)(nib - 8);
+}
+
+// RMSNorm of x (global, n floats) into hs (shared), cpu.go:81-98: the scale
+// 1/sqrt(mean + eps) in double, then (x * s) * w.
+__device__ __forceinline__ void rmsnorm_to_smem(const float *xs_in, const float *__restrict__ w, int n, float eps,
+                                                float *hs, float *red) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+        const float v = xs_in[i];
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, red);
+    const float t = __fadd_rn(__fdiv_rn(ss, (float)n), eps);
+    const float s = (float)(1.0 / sqrt((double)t));
+    for (int i = threadIdx.x; i < n; i += kThreads) hs[i] = __fmul_rn(__fmul_rn(xs_in[i], s), __ldg(w + i));
+    __syncthreads();
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// A grid-wide barrier over co-resident CTAs (the persistent kernel runs as
+// a cooperative launch).  The wait is bounded: after 2 s it records
+// DEV_BARRIER_TIMEOUT and returns false, as does every later barrier, so the
+// kernel ends instead of hanging.
+__device__ __noinline__ bool grid_sync(GridBarrier *bar, int *err) {
+    __shared__ int ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ok = 1;
+        const unsigned g = ld_acquire(&bar->gen);
+        __threadfence();
+        const unsigned arrived = atomicAdd(&bar->count, 1u);
+        if (arrived == gridDim.x - 1) {
+            bar->count = 0;
+            __threadfence();
+            st_release(&bar->gen, g + 1);
+        } else {
+            const uint64_t t0 = globaltimer();
+            while (ld_acquire(&bar->gen) == g) {
+                if (globaltimer() - t0 > 2000000000ull) {
+                    atomicExch(err, DEV_BARRIER_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        if (ok && *(volatile int *)err != 0) ok = 0;
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+// ------------------------------------------------------------- phases --
+// Work items are spread over CTAs first: tile i belongs to CTA i % ncta,
+// warp (i / ncta) % kWarps, so a phase with few tiles still uses many SMs.
+
+struct Smem {
+    float *vec;  // max(embd, ff) floats
+    float *red;  // reduction scratch
+};
+
+__device__ __forceinline__ bool cta_has_tiles(int cta, int ntiles) { return cta < ntiles; }
+
+// K1: RMSNorm + [Wq; Wk; Wv] + bias + RoPE + KV append for token t at
+// position pos (kernels_fused.go:47-73,212-224; cpu.go:279-303).  With
+// from_embed the residual is first taken from the embedding row of tok, and
+// CTA 0 writes it to x.
+__device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bool from_embed, int cta, int ncta,
+                          const Smem &sm) {
+    const Layer &L = dm.layer[l];
+    const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, nv = L.v.rows >> 3, total = nq + nk + nv;
+    if (!cta_has_tiles(cta, total)) return;
+    const int E = dm.embd, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *xrow = dm.x + (size_t)t * E;
+    float *xs = sm.vec + E;  // raw residual (second half of the buffer)
+    if (from_embed) {
+        for (int e = threadIdx.x; e < E; e += kThreads) {
+            const float v = gather(dm.embed, tok, e);
+            xs[e] = v;
+            if (cta == 0) xrow[e] = v;
+        }
+    } else {
+        for (int e = threadIdx.x; e < E; e += kThreads) xs[e] = __ldcg(xrow + e);
+    }
+    __syncthreads();
+    rmsnorm_to_smem(xs, L.attn_norm, E, dm.eps, sm.vec, sm.red);
+    const int hp = dm.head_dim >> 1;
+    for (int tile = cta + ncta * warp; tile < total; tile += ncta * kWarps) {
+        int seg, lt;
+        const QMat *m;
+        if (tile < nq) seg = 0, lt = tile, m = &L.q;
+        else if (tile < nq + nk) seg = 1, lt = tile - nq, m = &L.k;
+        else seg = 2, lt = tile - nq - nk, m = &L.v;
+        float a = tile_dot(*m, lt, sm.vec, lane);
+        const int r = lane >> 2, row = lt * 8 + r;
+        const float *bias = seg == 0 ? L.bq : seg == 1 ? L.bk : L.bv;
+        if (bias) a = __fadd_rn(a, __ldg(bias + row));
+        if (seg < 2) {  // rotate adjacent pairs (rows 2p, 2p+1 of a head), cpu.go:371-385
+            const float other = __shfl_xor_sync(kFull, a, 4);
+            const int p = (row % dm.head_dim) >> 1;
+            const float2 cs = __ldg(reinterpret_cast<const float2 *>(dm.rope_cs) + (size_t)pos * hp + p);
+            if ((r & 1) == 0) a = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(other, cs.y));
+            else a = __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(a, cs.x));
+        }
+        if ((lane & 3) == 0) {
+            if (seg == 0) dm.q[(size_t)t * E + row] = a;
+            else if (seg == 1) L.kv[(size_t)pos * dm.kvd + row] = a;
+            else L.kv[((size_t)dm.ctx + pos) * dm.kvd + row] = a;
+        }
+    }
+}
+
+// K2 + the merge of K3: attention of token t (n positions visible) for item
+// = (head, chunk of kAttnChunk positions): scores, chunk max and exp-sum,
+// exp-weighted V sum (kernels_fused.go:82-146).  The last CTA of a head to
+// finish merges the head's chunks (kernels_fused.go:150-170) into att.
+__device__ void phase_attn(const DevModel &dm, int l, int t, int n, int item, uint32_t *att_cnt, const Smem &sm) {
+    const int HD = dm.head_dim, grp = dm.heads / dm.kv_heads;
+    const int nch = (n + kAttnChunk - 1) / kAttnChunk;
+    const int h = item / nch, c = item % nch;
+    const int kvh = h / grp;
+    const Layer &L = dm.layer[l];
+    float *qh = sm.vec;              // HD
+    float *e = sm.vec + HD;          // kAttnChunk
+    float *part = sm.vec + HD + kAttnChunk;  // kThreads * 4 (partial V sums)
+    __shared__ int last;
+    for (int i = threadIdx.x; i < HD; i += kThreads) qh[i] = __ldcg(dm.q + (size_t)t * dm.embd + h * HD + i);
+    __syncthreads();
+    const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
+    // scores: 4 threads per position, HD/4 dims each
+    const int p = threadIdx.x >> 2, sub = threadIdx.x & 3;
+    float s = -FLT_MAX;
+    {
+        float part_s = 0.f;
+        if (p < cnt) {
+            const float *kr = L.kv + (size_t)(p0 + p) * dm.kvd + kvh * HD;
+            for (int d = sub * 4; d < HD; d += 16) {
+                const float4 k4 = __ldcg(reinterpret_cast<const float4 *>(kr + d));
+                part_s = fmaf(qh[d], k4.x, part_s);
+                part_s = fmaf(qh[d + 1], k4.y, part_s);
+                part_s = fmaf(qh[d + 2], k4.z, part_s);
+                part_s = fmaf(qh[d + 3], k4.w, part_s);
+            }
+        }
+        part_s += __shfl_xor_sync(kFull, part_s, 1);
+        part_s += __shfl_xor_sync(kFull, part_s, 2);
+        if (p < cnt) s = __fmul_rn(part_s, dm.scale);
+    }
+    const float mx = block_max(s, sm.red);
+    float ev = 0.f;
+    if (p < cnt && sub == 0) {
+        ev = (float)exp((double)__fsub_rn(s, mx));
+        e[p] = ev;
+    }
+    const float lsum = block_sum(ev, sm.red);  // includes the __syncthreads that publishes e[]
+    // V sum: thread (d4, g): float4 d4 of the head, positions g, g+G, ...
+    const int nd4 = HD / 4, G = kThreads / nd4;
+    const int d4 = threadIdx.x % nd4, g = threadIdx.x / nd4;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int pp = g; pp < cnt; pp += G) {
+        const float w = e[pp];
+        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(L.kv + ((size_t)dm.ctx + p0 + pp) * dm.kvd + kvh * HD) + d4);
+        o.x = fmaf(w, v4.x, o.x);
+        o.y = fmaf(w, v4.y, o.y);
+        o.z = fmaf(w, v4.z, o.z);
+        o.w = fmaf(w, v4.w, o.w);
+    }
+    reinterpret_cast<float4 *>(part)[threadIdx.x] = o;
+    __syncthreads();
+    const size_t th = (size_t)t * dm.heads + h;
+    if (threadIdx.x < nd4) {
+        float4 tot = reinterpret_cast<float4 *>(part)[threadIdx.x];
+        for (int k = 1; k < G; ++k) {
+            const float4 v = reinterpret_cast<float4 *>(part)[threadIdx.x + k * nd4];
+            tot.x += v.x, tot.y += v.y, tot.z += v.z, tot.w += v.w;
+        }
+        reinterpret_cast<float4 *>(dm.part_pv + (th * dm.nchunk + c) * HD)[threadIdx.x] = tot;
+    }
+    if (threadIdx.x == 0) dm.part_ml[th * dm.nchunk + c] = make_float2(mx, lsum);
+    // the last arriving CTA of this head merges its chunks
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(att_cnt + th, 1u);
+        last = prev == (unsigned)(nch - 1);
+        if (last) att_cnt[th] = 0;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int d = threadIdx.x; d < HD; d += kThreads) {
+        float M = -FLT_MAX;
+        for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(&dm.part_ml[th * dm.nchunk + cc].x));
+        float lt = 0.f, ot = 0.f;
+        for (int cc = 0; cc < nch; ++cc) {
+            const float2 ml = __ldcg(&dm.part_ml[th * dm.nchunk + cc]);
+            const float f = (float)exp((double)__fsub_rn(ml.x, M));
+            lt = fmaf(f, ml.y, lt);
+            ot = fmaf(f, __ldcg(dm.part_pv + (th * dm.nchunk + cc) * HD + d), ot);
+        }
+        const float a = __fdiv_rn(ot, lt);
+        dm.att[(size_t)t * dm.embd + h * HD + d] = a;
+    }
+}
+
+// K3's product: x += Wo att (cpu.go:336-339).
+__device__ void phase_oproj(const DevModel &dm, int l, int t, int cta, int ncta, const Smem &sm) {
+    const Layer &L = dm.layer[l];
+    const int ntiles = L.o.rows >> 3;
+    if (!cta_has_tiles(cta, ntiles)) return;
+    const int E = dm.embd, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < E; i += kThreads) sm.vec[i] = __ldcg(dm.att + (size_t)t * E + i);
+    __syncthreads();
+    float *xrow = dm.x + (size_t)t * E;
+    for (int tile = cta + ncta * warp; tile < ntiles; tile += ncta * kWarps) {
+        const float a = tile_dot(L.o, tile, sm.vec, lane);
+        const int row = tile * 8 + (lane >> 2);
+        if ((lane & 3) == 0) xrow[row] = __fadd_rn(__ldcg(xrow + row), a);
+    }
+}
+
+// K4: RMSNorm + [Wgate; Wup] + SwiGLU (kernels_fused.go:28-42; cpu.go
+// :340-346): act = g / (1 + exp(-g)) * u, exp in double.
+__device__ void phase_gateup(const DevModel &dm, int l, int t, int cta, int ncta, const Smem &sm) {
+    const Layer &L = dm.layer[l];
+    const int ntiles = L.gate.rows >> 3;
+    if (!cta_has_tiles(cta, ntiles)) return;
+    const int E = dm.embd, F = dm.ff, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *xs = sm.vec + E;
+    for (int e = threadIdx.x; e < E; e += kThreads) xs[e] = __ldcg(dm.x + (size_t)t * E + e);
+    __syncthreads();
+    rmsnorm_to_smem(xs, L.ffn_norm, E, dm.eps, sm.vec, sm.red);
+    for (int tile = cta + ncta * warp; tile < ntiles; tile += ncta * kWarps) {
+        const float g = tile_dot(L.gate, tile, sm.vec, lane);
+        const float u = tile_dot(L.up, tile, sm.vec, lane);
+        const int row = tile * 8 + (lane >> 2);
+        if ((lane & 3) == 0 && row < F) {
+            const float den = __fadd_rn(1.f, (float)exp(-(double)g));
+            dm.act[(size_t)t * F + row] = __fmul_rn(__fdiv_rn(g, den), u);
+        }
+    }
+}
+
+// K5: x += Wdown act (cpu.go:347-350).
+__device__ void phase_down(const DevModel &dm, int l, int t, int cta, int ncta, const Smem &sm) {
+    const Layer &L = dm.layer[l];
+    const int ntiles = L.down.rows >> 3;
+    if (!cta_has_tiles(cta, ntiles)) return;
+    const int E = dm.embd, F = dm.ff, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < F; i += kThreads) sm.vec[i] = __ldcg(dm.act + (size_t)t * F + i);
+    __syncthreads();
+    float *xrow = dm.x + (size_t)t * E;
+    for (int tile = cta + ncta * warp; tile < ntiles; tile += ncta * kWarps) {
+        const float a = tile_dot(L.down, tile, sm.vec, lane);
+        const int row = tile * 8 + (lane >> 2);
+        if ((lane & 3) == 0) xrow[row] = __fadd_rn(__ldcg(xrow + row), a);
+    }
+}
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+// The head: RMSNorm(output_norm) of token t's residual, logits = Wout h
+// (cpu.go:357-363), and this CTA's argmax partial (value, index).
+__device__ void phase_head(const DevModel &dm, int t, int cta, int ncta, const Smem &sm) {
+    const int E = dm.embd, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int ntiles = dm.head.rows >> 3;
+    float *xs = sm.vec + E;
+    for (int e = threadIdx.x; e < E; e += kThreads) xs[e] = __ldcg(dm.x + (size_t)t * E + e);
+    __syncthreads();
+    rmsnorm_to_smem(xs, dm.out_norm, E, dm.eps, sm.vec, sm.red);
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    for (int tile = cta + ncta * warp; tile < ntiles; tile += ncta * kWarps) {
+        const float a = tile_dot(dm.head, tile, sm.vec, lane);
+        const int row = tile * 8 + (lane >> 2);
+        if (row < dm.vocab) {
+            if ((lane & 3) == 0) dm.logits[row] = a;
+            if (better(a, row, bv, bi)) bv = a, bi = row;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bv, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (better(ov, oi, bv, bi)) bv = ov, bi = oi;
+    }
+    __shared__ float wv[kWarps];
+    __shared__ int wi[kWarps];
+    if (lane == 0) wv[warp] = bv, wi[warp] = bi;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kWarps; ++w)
+            if (better(wv[w], wi[w], bv, bi)) bv = wv[w], bi = wi[w];
+        dm.am_part[cta] = make_float2(bv, __int_as_float(bi));
+    }
+}
+
+// The argmax over the CTAs' partials (first index of the largest value).
+__device__ __forceinline__ int reduce_argmax(const DevModel &dm, int nparts, float *red) {
+    __shared__ int result;
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < nparts; i += kThreads) {
+        const float2 p = __ldcg(dm.am_part + i);
+        const int pi = __float_as_int(p.y);
+        if (better(p.x, pi, bv, bi)) bv = p.x, bi = pi;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bv, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (better(ov, oi, bv, bi)) bv = ov, bi = oi;
+    }
+    __shared__ float wv[kWarps];
+    __shared__ int wi[kWarps];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) wv[warp] = bv, wi[warp] = bi;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kWarps; ++w)
+            if (better(wv[w], wi[w], bv, bi)) bv = wv[w], bi = wi[w];
+        result = bi == 0x7fffffff ? 0 : bi;
+    }
+    __syncthreads();
+    return result;
+}
+
+__device__ __forceinline__ Smem smem_views(float *base, const DevModel &dm) { return Smem{base, base + dm.smem_vec}; }
+
+// ---------------------------------------------------- per-phase kernels --
+
+__global__ void __launch_bounds__(kThreads) k_embed(const DevModel *__restrict__ dmp) {
+    const DevModel &dm = *dmp;
+    const int t = blockIdx.x;
+    const int tok = dm.tokens[dm.state[1] + t];
+    for (int e = threadIdx.x; e < dm.embd; e += kThreads) dm.x[(size_t)t * dm.embd + e] = gather(dm.embed, tok, e);
+}
+
+__global__ void __launch_bounds__(kThreads) k_qkv(const DevModel *__restrict__ dmp, int l) {
+    extern __shared__ float smem[];
+    const DevModel &dm = *dmp;
+    const int t = blockIdx.y;
+    const int pos = dm.state[0] + t, tok = l == 0 ? dm.tokens[dm.state[1] + t] : 0;
+    phase_qkv(dm, l, t, pos, tok, l == 0, blockIdx.x, gridDim.x, smem_views(smem, dm));
+}
+
+__global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ dmp, int l) {
+    extern __shared__ float smem[];
+    const DevModel &dm = *dmp;
+    const int t = blockIdx.y;
+    const int n = dm.state[0] + t + 1;
+    const int nch = (n + kAttnChunk - 1) / kAttnChunk;
+    if ((int)blockIdx.x >= dm.heads * nch) return;
+    phase_attn(dm, l, t, n, blockIdx.x, dm.att_cnt, smem_views(smem, dm));
+}
+
+__global__ void __launch_bounds__(kThreads) k_oproj(const DevModel *__restrict__ dmp, int l) {
+    extern __shared__ float smem[];
+    phase_oproj(*dmp, l, blockIdx.y, blockIdx.x, gridDim.x, smem_views(smem, *dmp));
+}
+
+__global__ void __launch_bounds__(kThreads) k_gateup(const DevModel *__restrict__ dmp, int l) {
+    extern __shared__ float smem[];
+    phase_gateup(*dmp, l, blockIdx.y, blockIdx.x, gridDim.x, smem_views(smem, *dmp));
+}
+
+__global__ void __launch_bounds__(kThreads) k_down(const DevModel *__restrict__ dmp, int l) {
+    extern __shared__ float smem[];
+    phase_down(*dmp, l, blockIdx.y, blockIdx.x, gridDim.x, smem_views(smem, *dmp));
+}
+
+// The head and the argmax: the last CTA to finish reduces the partials,
+// writes the token and advances the state (kernels.go:354-415).
+__global__ void __launch_bounds__(kThreads) k_head(const DevModel *__restrict__ dmp, int t_src, int adv) {
+    extern __shared__ float smem[];
+    const DevModel &dm = *dmp;
+    Smem sm = smem_views(smem, dm);
+    phase_head(dm, t_src, blockIdx.x, gridDim.x, sm);
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(dm.am_count, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int tok = reduce_argmax(dm, gridDim.x, sm.red);
+    if (threadIdx.x == 0) {
+        *dm.am_count = 0;
+        const uint32_t step = dm.state[1] + adv;
+        dm.tokens[step] = tok;
+        dm.state[0] += adv;
+        dm.state[1] = step;
+    }
+}
+
+__global__ void k_advance(const DevModel *__restrict__ dmp, int n) {
+    dmp->state[0] += n;
+    dmp->state[1] += n;
+}
+
+// ------------------------------------------------ the persistent kernel --
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_decode(const DevModel *__restrict__ dmp, GridBarrier *bar, int ntok) {
+    extern __shared__ float smem[];
+    const DevModel &dm = *dmp;
+    Smem sm = smem_views(smem, dm);
+    const int cta = blockIdx.x, ncta = gridDim.x;
+    int pos = (int)__ldcg(dm.state), step = (int)__ldcg(dm.state + 1);
+    int tok = __ldcg(dm.tokens + step);
+    for (int i = 0; i < ntok; ++i) {
+        if (pos >= dm.ctx) {
+            if (cta == 0 && threadIdx.x == 0) atomicExch(dm.err, DEV_CONTEXT_FULL);
+            return;
+        }
+        const int n = pos + 1, nch = (n + kAttnChunk - 1) / kAttnChunk;
+        for (int l = 0; l < dm.layers; ++l) {
+            phase_qkv(dm, l, 0, pos, tok, l == 0, cta, ncta, sm);
+            if (!grid_sync(bar, dm.err)) return;
+            for (int item = cta; item < dm.heads * nch; item += ncta) {
+                phase_attn(dm, l, 0, n, item, dm.att_cnt, sm);
+                __syncthreads();
+            }
+            if (!grid_sync(bar, dm.err)) return;
+            phase_oproj(dm, l, 0, cta, ncta, sm);
+            if (!grid_sync(bar, dm.err)) return;
+            phase_gateup(dm, l, 0, cta, ncta, sm);
+            if (!grid_sync(bar, dm.err)) return;
+            phase_down(dm, l, 0, cta, ncta, sm);
+            if (!grid_sync(bar, dm.err)) return;
+        }
+        phase_head(dm, 0, cta, ncta, sm);
+        if (!grid_sync(bar, dm.err)) return;
+        tok = reduce_argmax(dm, ncta, sm.red);
+        ++pos, ++step;
+        if (cta == 0 && threadIdx.x == 0) dm.tokens[step] = tok;
+        // every CTA reads the partials before any CTA of the next token
+        // overwrites them (its head phase comes after 5 * layers barriers)
+    }
+    if (cta == 0 && threadIdx.x == 0) {
+        dm.state[0] = pos;
+        dm.state[1] = step;
+    }
+}
+
+// ------------------------------------------------------------ loading --
+
+__device__ __forceinline__ int neox_map(int nr, int hd) {  // fused.go:331-334
+    const int h = nr / hd, k = nr % hd;
+    return h * hd + k / 2 + (k % 2) * (hd / 2);
+}
+
+__global__ void k_repack(const uint8_t *__restrict__ raw, int rows, int nb, int type, uint8_t *__restrict__ tiles,
+                         int tile_bytes, int dst_row0, int neox_hd) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)rows * nb) return;
+    const int rr = (int)(idx / nb), b = (int)(idx % nb);
+    const int src = neox_hd > 0 ? neox_map(rr, neox_hd) : rr;
+    const int bb = type == 8 ? 34 : type == 3 ? 20 : 18;
+    const int qb = type == 8 ? 32 : 16, qoff = type == 3 ? 4 : 2;
+    const uint8_t *blk = raw + ((size_t)src * nb + b) * bb;
+    const int drow = dst_row0 + rr, r = drow & 7;
+    uint8_t *tp = tiles + (size_t)(drow >> 3) * tile_bytes;
+    uint8_t *qd = tp + ((size_t)b * 8 + r) * qb;
+    for (int j = 0; j < qb; ++j) qd[j] = blk[qoff + j];
+    uint8_t *dd = tp + (size_t)nb * 8 * qb + ((size_t)b * 8 + r) * 2;
+    dd[0] = blk[0], dd[1] = blk[1];
+    if (type == 3) {
+        uint8_t *md = tp + (size_t)nb * 8 * qb + (size_t)nb * 16 + ((size_t)b * 8 + r) * 2;
+        md[0] = blk[2], md[1] = blk[3];
+    }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------- launchers --
+
+int smem_vec_floats(const Shapes &s) {
+    const int vec = s.embd + (s.embd > s.ff ? s.embd : s.ff);
+    const int attn = s.head_dim + kAttnChunk + 4 * kThreads;
+    return vec > attn ? vec : attn;
+}
+
+size_t smem_bytes(const Shapes &s) { return ((size_t)smem_vec_floats(s) + 2 * kWarps) * sizeof(float); }
+
+void launch_repack(const uint8_t *raw, int rows, int nb, int type, uint8_t *tiles, int tile_bytes, int dst_row0,
+                   int neox_hd, cudaStream_t st) {
+    const int64_t n = (int64_t)rows * nb;
+    k_repack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, rows, nb, type, tiles, tile_bytes, dst_row0, neox_hd);
+}
+
+void launch_embed(const DevModel *dm, const Shapes &s, int m, cudaStream_t st) {
+    k_embed<<<m, kThreads, 0, st>>>(dm);
+}
+
+static inline unsigned ctas_for(int tiles) { return (unsigned)((tiles + kWarps - 1) / kWarps); }
+
+void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st) {
+    const size_t sh = smem_bytes(s);
+    k_qkv<<<dim3(ctas_for(s.qkv_tiles), m), kThreads, sh, st>>>(dm, l);
+    k_attn<<<dim3(s.heads * s.nchunk, m), kThreads, sh, st>>>(dm, l);
+    k_oproj<<<dim3(ctas_for(s.o_tiles), m), kThreads, sh, st>>>(dm, l);
+    k_gateup<<<dim3(ctas_for(s.gu_tiles), m), kThreads, sh, st>>>(dm, l);
+    k_down<<<dim3(ctas_for(s.down_tiles), m), kThreads, sh, st>>>(dm, l);
+}
+
+void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaStream_t st) {
+    k_head<<<s.head_ctas, kThreads, smem_bytes(s), st>>>(dm, t_src, adv);
+}
+
+void launch_advance(const DevModel *dm, int n, cudaStream_t st) { k_advance<<<1, 1, 0, st>>>(dm, n); }
+
+int persistent_ctas_per_sm(const Shapes &s) {
+    int n = 0;
+    const size_t sh = smem_bytes(s);
+    cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode, kThreads, sh);
+    return n;
+}
+
+cudaError_t launch_decode_persistent(const DevModel *dm, const Shapes &s, GridBarrier *bar, int ntok, int ctas,
+                                     cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes(s);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_decode, dm, bar, ntok);
+}
+
+}  // namespace llmb

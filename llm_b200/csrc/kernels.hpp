@@ -1,0 +1,67 @@
+// Host-side launchers of the forward-pass kernels (kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "device.hpp"
+
+namespace llmb {
+
+// Device error codes written to DevModel::err.
+enum DeviceError : int {
+    DEV_OK = 0,
+    DEV_BARRIER_TIMEOUT = 1,  // a grid barrier waited longer than its limit
+    DEV_CONTEXT_FULL = 2,     // a token past the context
+};
+
+struct GridBarrier {
+    unsigned int count;
+    unsigned int gen;
+};
+
+// Host copy of what launch shapes need.
+struct Shapes {
+    int embd, ff, heads, kv_heads, head_dim, kvd, vocab, ctx, layers, nchunk;
+    int qkv_tiles, o_tiles, gu_tiles, down_tiles, head_tiles;
+    int head_ctas;  // CTAs of the head kernel (argmax partials)
+};
+
+constexpr int kWarps = 8;             // warps per CTA
+constexpr int kThreads = kWarps * 32; // threads per CTA
+
+// Dynamic shared memory of every kernel: a vector region, then reduction scratch.
+int smem_vec_floats(const Shapes &s);
+size_t smem_bytes(const Shapes &s);
+
+// Repacks `rows` raw GGUF rows (blocks of `type`) staged in device memory
+// into the tile layout at destination row dst_row0.  neox_hd > 0 reorders the
+// rows of each head of neox_hd rows from the NEOX layout to adjacent pairs
+// (fused.go:329-344): destination row nr takes source row neoxMap(nr).
+void launch_repack(const uint8_t *raw, int rows, int nb, int type, uint8_t *tiles, int tile_bytes, int dst_row0,
+                   int neox_hd, cudaStream_t st);
+
+// The embedding rows of m tokens into x (the layer-0 kernels fold this in;
+// used alone when no layer runs).
+void launch_embed(const DevModel *dm, const Shapes &s, int m, cudaStream_t st);
+
+// One layer for m tokens at positions state.pos .. state.pos+m-1 (5 kernels:
+// norm+QKV+bias+RoPE+KV append, attention partials and merge, output
+// projection + residual, norm+gate/up+SwiGLU, down + residual).
+void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st);
+
+// Final norm of token t_src's residual, the vocab logits, and the argmax:
+// writes tokens[state.step + adv] and advances state by adv.
+void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaStream_t st);
+
+// state += n.
+void launch_advance(const DevModel *dm, int n, cudaStream_t st);
+
+// The persistent decode kernel: ntok tokens, every phase of every layer and
+// the head, one cooperative launch over all SMs with bounded grid barriers.
+cudaError_t launch_decode_persistent(const DevModel *dm, const Shapes &s, GridBarrier *bar, int ntok, int ctas,
+                                     cudaStream_t st);
+
+// CTAs per SM the persistent kernel can keep resident (for the cooperative grid).
+int persistent_ctas_per_sm(const Shapes &s);
+
+}  // namespace llmb
