@@ -143,7 +143,8 @@ LLMB_API int llmb_generate_logits(llmb_model *m, const int32_t *prompt, int n_pr
 /* Peek, gpu.go:1016-1043: the first n 32-bit words of a named device buffer,
  * as floats.  Names: "x" (residual stream), "q", "att", "gate" (the SwiGLU
  * output), "logits", "state" ({position, step} as raw bits), "tokens",
- * and "kvblk.N." (layer N's cache: K then V). */
+ * "kvblk.N." (layer N's cache: K then V) and, with the decode_trace knob,
+ * "trace" (64-bit globaltimer stamps, see the knob). */
 LLMB_API int llmb_peek(llmb_model *m, const char *name, float *out, int n);
 
 /* GPU.Layers, gpu.go:143-146: run only that many layers (debugging: no
@@ -156,8 +157,10 @@ LLMB_API int llmb_set_layers(llmb_model *m, int layers);
  * (Limits.MemoryBudget, gpu.go:35; bytes, 0 = the device's free memory;
  * read by llmb_open).  One more, with no counterpart in the reference:
  * "decode_mode" 0 (default) decodes with the persistent kernel, 1 with one
- * kernel per phase (an A/B and debugging aid).  Process-wide, like the Go
- * package variables. */
+ * kernel per phase (an A/B and debugging aid); "decode_trace" 1 makes models
+ * opened afterwards record the persistent kernel's phase timeline, read with
+ * llmb_peek(m, "trace", ...) (a profiling aid, the counterpart of GPU.Skip,
+ * gpu.go:769-784).  Process-wide, like the Go package variables. */
 LLMB_API int llmb_set_knob(const char *name, int64_t value);
 LLMB_API int64_t llmb_get_knob(const char *name);
 

@@ -1,0 +1,1146 @@
+// The persistent decode kernel: DecodeBatch tokens of batch-1 greedy decoding
+// in one cooperative launch over every SM (Generate's decode submits,
+// gpu.go:987-1009, and the per-token pass, gpu.go:792-832, fused.go:259-289).
+//
+// Structure of a CTA (one per SM):
+//   - a producer warp streams the CTA's weight tiles, in the order the CTA
+//     consumes them, through a ring of shared-memory slots with 1D bulk TMA
+//     copies (cp.async.bulk, no multicast) tracked by mbarriers.  Weights do
+//     not depend on activations, so the stream runs ahead across phases,
+//     layers and tokens as far as the ring allows;
+//   - 8 consumer warps compute.  Every tile's blocks are split across the
+//     warps; each warp accumulates its partial row sums in double across
+//     blocks (a block's 8-term sums in paired f32), and the partials meet in
+//     shared memory in a fixed order, so results are deterministic.
+//
+// Activations move between CTAs as 64-bit words {f32 value, u32 tag}
+// written and polled with relaxed GPU-scope accesses (a value and its tag
+// are one single-copy-atomic store, so a reader that sees the tag sees the
+// value): each CTA waits only for the vector it needs, with no grid-wide
+// barrier between phases.  A tag is unique per (token, layer, phase)
+// across calls (a device epoch counter).  One fenced grid barrier per token
+// publishes the argmax partials and the token's KV-cache rows.
+//
+// Every wait (mbarrier, tag poll, grid barrier) is bounded: past its limit
+// the kernel records an error in DevModel::err and returns; the producer
+// first waits (bounded) for its copies in flight.
+#include <cuda_fp16.h>
+
+#include <cfloat>
+#include <cstdint>
+
+#include "kernels.hpp"
+
+namespace llmb {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kCons = 8;                 // consumer warps
+constexpr int kConsThreads = kCons * 32; // 256
+constexpr int kDecThreads = kConsThreads + 32;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+
+// ------------------------------------------------------------ primitives --
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+
+// 1D bulk copy global -> this CTA's shared memory, completing on mbarrier b.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *b) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(b))
+                 : "memory");
+}
+
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsThreads) : "memory"); }
+
+// A consumer barrier that also ORs a predicate over the consumer threads, so
+// that every thread takes the same branch after it (a thread that left a
+// named barrier early would leave the others waiting).
+__device__ __forceinline__ bool cons_or(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "n"(kConsThreads)
+        : "memory");
+    return r != 0;
+}
+
+// Two consecutive tagged words (each single-copy atomic on its own).
+__device__ __forceinline__ void ld_relaxed2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void ll_put(uint64_t *p, float v, uint32_t tag) {
+    st_relaxed(p, (uint64_t)tag << 32 | __float_as_uint(v));
+}
+
+__device__ __forceinline__ int read_err(const int *e) { return *(volatile const int *)e; }
+
+// A tagged vector to poll into shared memory: src[0, n) (n even), tag, dst.
+struct Seg {
+    const uint64_t *src;
+    int n;
+    uint32_t tag;
+    float *dst;
+};
+
+// Polls up to 3 tagged vectors.  Each consumer thread owns word pairs t,
+// t + 256, ... of their concatenation and issues the loads of up to 4 pairs
+// before testing any, so the vectors cost about one round trip per 1024
+// pairs, not one per value.
+__device__ __forceinline__ const uint64_t *seg_src(const Seg *sg, int ns, int i, int &j, int &lo) {
+    lo = 0;
+    for (j = 0; j < ns; ++j) {
+        const int np = sg[j].n >> 1;
+        if (i < lo + np) return sg[j].src + 2 * (i - lo);
+        lo += np;
+    }
+    return nullptr;
+}
+
+template <int NS>
+__device__ __noinline__ bool poll_segs(const Seg (&sg)[NS], int *err) {
+    int npairs = 0;
+#pragma unroll
+    for (int j = 0; j < NS; ++j) npairs += sg[j].n >> 1;
+    constexpr int K = 4;
+    for (int base = 0; base < npairs; base += K * kConsThreads) {
+        uint64_t v[2 * K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            int j, lo;
+            const uint64_t *p = seg_src(sg, NS, base + threadIdx.x + k * kConsThreads, j, lo);
+            if (p) ld_relaxed2(p, v[2 * k], v[2 * k + 1]);
+        }
+        const uint64_t t0 = gtimer();
+        unsigned spins = 0;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int i = base + threadIdx.x + k * kConsThreads;
+            int j, lo;
+            const uint64_t *p = seg_src(sg, NS, i, j, lo);
+            if (!p) continue;
+            const uint32_t tag = sg[j].tag;
+            while ((uint32_t)(v[2 * k] >> 32) != tag || (uint32_t)(v[2 * k + 1] >> 32) != tag) {
+                ld_relaxed2(p, v[2 * k], v[2 * k + 1]);
+                if ((++spins & 255) == 0) {
+                    if (read_err(err)) return false;
+                    if (gtimer() - t0 > kWaitNs) {
+                        atomicExch(err, DEV_TAG_TIMEOUT);
+                        return false;
+                    }
+                }
+            }
+            float *d = sg[j].dst + 2 * (i - lo);
+            d[0] = __uint_as_float((uint32_t)v[2 * k]);
+            d[1] = __uint_as_float((uint32_t)v[2 * k + 1]);
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool poll_vec(const uint64_t *src, int n, uint32_t tag, float *dst, int *err) {
+    const Seg sg[1] = {{src, n, tag, dst}};
+    return poll_segs(sg, err);
+}
+
+__device__ __forceinline__ bool poll_two(const uint64_t *a, int na, uint32_t ta, float *da, const uint64_t *b, int nb,
+                                         uint32_t tb, float *db, int *err) {
+    const Seg sg[2] = {{a, na, ta, da}, {b, nb, tb, db}};
+    return poll_segs(sg, err);
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Fenced grid barrier among the consumer threads of all CTAs.
+__device__ bool grid_sync_cons(GridBarrier *bar, int *err) {
+    __shared__ int ok;
+    cons_sync();
+    if (threadIdx.x == 0) {
+        ok = 1;
+        const unsigned g = ld_acquire(&bar->gen);
+        __threadfence();
+        const unsigned arrived = atomicAdd(&bar->count, 1u);
+        if (arrived == gridDim.x - 1) {
+            bar->count = 0;
+            __threadfence();
+            st_release(&bar->gen, g + 1);
+        } else {
+            const uint64_t t0 = gtimer();
+            while (ld_acquire(&bar->gen) == g) {
+                if (read_err(err)) {
+                    ok = 0;
+                    break;
+                }
+                if (gtimer() - t0 > kWaitNs) {
+                    atomicExch(err, DEV_BARRIER_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        __threadfence();
+    }
+    cons_sync();
+    return ok != 0;
+}
+
+__device__ __forceinline__ float b2f(uint32_t v, int k) {
+    return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | k));
+}
+
+// Phase timeline (DevModel::trace): for event ev of this CTA, stamps 0..2
+// (entry, input ready, exit) and the time the phase spent waiting for weight
+// slots (field 3, accumulated by unit_rows).
+__shared__ uint64_t s_ring_wait;
+
+struct Trace {
+    uint64_t *p;  // this CTA's events, or null
+    __device__ void stamp(int ev, int k) const {
+        if (p && threadIdx.x == 0) {
+            p[ev * 4 + k] = gtimer();
+            if (k == 2) p[ev * 4 + 3] = s_ring_wait, s_ring_wait = 0;
+        }
+    }
+};
+
+// ------------------------------------------------------------ schedule --
+// The CTA's share of a matrix: tiles [a, b) (contiguous), in units of at most
+// `per` tiles (one bulk copy each, at most one slot).
+
+struct Share {
+    int a, b, per;
+};
+
+__device__ __forceinline__ Share share(const QMat &m, int cta, int ncta, int slot_bytes) {
+    const int T = m.rows >> 3;
+    const int P = min(ncta, T);
+    Share s;
+    if (cta < P) {
+        s.a = (int)((int64_t)T * cta / P);
+        s.b = (int)((int64_t)T * (cta + 1) / P);
+    } else {
+        s.a = s.b = 0;
+    }
+    s.per = max(1, min(kConsThreads / 8, slot_bytes / m.tile_bytes));
+    return s;
+}
+
+// --------------------------------------------------------- smem layout --
+
+struct DecSmem {
+    uint64_t *full, *empty;  // ring mbarriers
+    uint8_t *ring;           // nslots * slot_bytes
+    float *xv;               // activation vector, paired layout for Q4 / plain for Q8 (max(E,F) floats)
+    float *xq8;              // the same vector in plain layout when a Q8_0 matrix reads it
+    float *xs;               // raw residual (E floats)
+    double *part;            // [kCons][8 tiles-in-unit max 8][8 rows] partial sums
+    float *rows;             // row results of a unit [64]
+    float *gate;             // gate rows of this CTA's gate/up share (max 8 * 64 rows)
+    float *red;              // reduction scratch [64]
+    float *att;              // attention scratch
+    float *merge;            // attention partials of up to 8 chunks: pv [8][E], then (max, sum) [8][H]
+    float *pre;              // the QKV epilogue's bias and RoPE (cos, sin) per row of the CTA's share
+    float *kvs;              // an attention item's history K and V rows [2][kAttnChunk][head_dim]
+};
+
+// --------------------------------------------------------- dot products --
+// A tile of 8 rows in shared memory; lane (r, q) = (lane / 4, lane % 4).
+// Returns the lane's partial over blocks [b0, b1), in double.
+
+// Q4_0 / Q4_1 with the activation in paired layout: for block b, pair j
+// (0..15) = (x[32b + j], x[32b + 16 + j]), so lane q reads pairs 4q..4q+3.
+template <bool Q41>
+__device__ __forceinline__ double dot_q4(const uint8_t *tile, int nb, const float2 *xp, int b0, int b1, int lane) {
+    const int r = lane >> 2, q = lane & 3;
+    const uint32_t *qw = reinterpret_cast<const uint32_t *>(tile) + r * 4 + q;
+    const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 128) + r;
+    const __half *mp = dp + nb * 8;
+    const float off = Q41 ? 8388608.f : 8388616.f;
+    const float2 off2 = make_float2(off, off);
+    double acc = 0.0;
+#pragma unroll 4
+    for (int b = b0; b < b1; ++b) {
+        const uint32_t w = qw[b * 32];
+        const float d = __half2float(dp[b * 8]);
+        const float4 xa = reinterpret_cast<const float4 *>(xp)[b * 8 + 2 * q];
+        const float4 xb = reinterpret_cast<const float4 *>(xp)[b * 8 + 2 * q + 1];
+        const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+        float2 s = __fmul2_rn(__fadd2_rn(make_float2(b2f(lo, 0), b2f(hi, 0)), make_float2(-off2.x, -off2.y)),
+                              make_float2(xa.x, xa.y));
+        s = __ffma2_rn(__fadd2_rn(make_float2(b2f(lo, 1), b2f(hi, 1)), make_float2(-off, -off)),
+                       make_float2(xa.z, xa.w), s);
+        s = __ffma2_rn(__fadd2_rn(make_float2(b2f(lo, 2), b2f(hi, 2)), make_float2(-off, -off)),
+                       make_float2(xb.x, xb.y), s);
+        s = __ffma2_rn(__fadd2_rn(make_float2(b2f(lo, 3), b2f(hi, 3)), make_float2(-off, -off)),
+                       make_float2(xb.z, xb.w), s);
+        const float sum = s.x + s.y;
+        if (Q41) {
+            const float mn = __half2float(mp[b * 8]);
+            const float2 sx2 = __fadd2_rn(__fadd2_rn(make_float2(xa.x, xa.y), make_float2(xa.z, xa.w)),
+                                          __fadd2_rn(make_float2(xb.x, xb.y), make_float2(xb.z, xb.w)));
+            acc = fma((double)d, (double)sum, fma((double)mn, (double)(sx2.x + sx2.y), acc));
+        } else {
+            acc = fma((double)d, (double)sum, acc);
+        }
+    }
+    return acc;
+}
+
+// Q8_0 with the activation in plain layout: lane q owns elements 8q..8q+7.
+__device__ __forceinline__ double dot_q8(const uint8_t *tile, int nb, const float *x, int b0, int b1, int lane) {
+    const int r = lane >> 2, q = lane & 3;
+    const uint2 *qw = reinterpret_cast<const uint2 *>(tile) + r * 4 + q;
+    const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 256) + r;
+    constexpr float off = 8388736.f;
+    double acc = 0.0;
+#pragma unroll 4
+    for (int b = b0; b < b1; ++b) {
+        const uint2 w = qw[b * 32];
+        const float d = __half2float(dp[b * 8]);
+        const float4 xa = reinterpret_cast<const float4 *>(x)[b * 8 + 2 * q];
+        const float4 xb = reinterpret_cast<const float4 *>(x)[b * 8 + 2 * q + 1];
+        const uint32_t u0 = w.x ^ 0x80808080u, u1 = w.y ^ 0x80808080u;
+        const float2 o2 = make_float2(-off, -off);
+        float2 s = __fmul2_rn(__fadd2_rn(make_float2(b2f(u0, 0), b2f(u0, 1)), o2), make_float2(xa.x, xa.y));
+        s = __ffma2_rn(__fadd2_rn(make_float2(b2f(u0, 2), b2f(u0, 3)), o2), make_float2(xa.z, xa.w), s);
+        s = __ffma2_rn(__fadd2_rn(make_float2(b2f(u1, 0), b2f(u1, 1)), o2), make_float2(xb.x, xb.y), s);
+        s = __ffma2_rn(__fadd2_rn(make_float2(b2f(u1, 2), b2f(u1, 3)), o2), make_float2(xb.z, xb.w), s);
+        acc = fma((double)d, (double)(s.x + s.y), acc);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ double dot_tile(int type, const uint8_t *tile, int nb, const DecSmem &sm, int b0, int b1,
+                                           int lane) {
+    if (type == 8) return dot_q8(tile, nb, sm.xq8, b0, b1, lane);
+    if (type == 3) return dot_q4<true>(tile, nb, reinterpret_cast<const float2 *>(sm.xv), b0, b1, lane);
+    return dot_q4<false>(tile, nb, reinterpret_cast<const float2 *>(sm.xv), b0, b1, lane);
+}
+
+// ------------------------------------------------------------- staging --
+// Writes v (n floats, in shared memory at `src`) into the layouts the dot
+// products read: paired for Q4 (xv) and, if needed, plain for Q8 (xq8).
+__device__ __forceinline__ void stage_vector(const float *src, int n, const DecSmem &sm, bool q8) {
+    const int t = threadIdx.x;
+    for (int i = t; i < n; i += kConsThreads) {
+        const float v = src[i];
+        const int b = i >> 5, j = i & 31;
+        const int pj = j & 15;
+        sm.xv[b * 32 + 2 * pj + (j >> 4)] = v;
+        if (q8) sm.xq8[i] = v;
+    }
+}
+
+__device__ __forceinline__ float cons_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    cons_sync();
+    if (l == 0) red[w] = v;
+    cons_sync();
+    float t = l < kCons ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
+    return t;
+}
+
+__device__ __forceinline__ float cons_max(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    cons_sync();
+    if (l == 0) red[w] = v;
+    cons_sync();
+    float t = l < kCons ? red[l] : -FLT_MAX;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t = fmaxf(t, __shfl_xor_sync(kFull, t, o));
+    return t;
+}
+
+// A consumer thread's norm weights (elements t, t + 256, ..., embd <= 1024),
+// loaded before the phase waits for its input, off the critical path.
+struct NormW {
+    float w[4];
+    __device__ void load(const float *wp, int E) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = threadIdx.x + k * kConsThreads;
+            w[k] = i < E ? __ldg(wp + i) : 0.f;
+        }
+    }
+};
+
+// RMSNorm (cpu.go:81-98) of sm.xs (E floats) with weights nw into the staging layouts.
+__device__ __forceinline__ void norm_stage(const DecParams &dm, const NormW &nw, const DecSmem &sm, bool q8) {
+    const int E = dm.embd;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < E; i += kConsThreads) ss = fmaf(sm.xs[i], sm.xs[i], ss);
+    ss = cons_sum(ss, sm.red);
+    const float t = __fadd_rn(__fdiv_rn(ss, (float)E), dm.eps);
+    const float s = (float)(1.0 / sqrt((double)t));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = threadIdx.x + k * kConsThreads;
+        if (i >= E) break;
+        const float v = __fmul_rn(__fmul_rn(sm.xs[i], s), nw.w[k]);
+        const int b = i >> 5, j = i & 31, pj = j & 15;
+        sm.xv[b * 32 + 2 * pj + (j >> 4)] = v;
+        if (q8) sm.xq8[i] = v;
+    }
+    cons_sync();
+}
+
+// ------------------------------------------------------------- consume --
+// The consumer side of the ring: waits for the next unit's slot.
+
+struct Ring {
+    int nslots, slot_bytes;
+    unsigned u;  // units consumed so far
+};
+
+__device__ __forceinline__ bool ring_wait(const DecSmem &sm, const Ring &rg, int *err) {
+    const int slot = rg.u % rg.nslots;
+    const unsigned parity = (rg.u / rg.nslots) & 1;
+    if (mbar_try_wait(sm.full + slot, parity)) return true;
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(sm.full + slot, parity)) {
+        if (read_err(err)) return false;
+        if (gtimer() - t0 > kWaitNs) {
+            atomicExch(err, DEV_RING_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void ring_release(const DecSmem &sm, Ring &rg) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(sm.empty + rg.u % rg.nslots);
+    rg.u++;
+}
+
+// Computes the rows of one unit (k tiles of matrix m, the first is tile t0)
+// into sm.rows[k * 8] (row i of the unit).  All consumer warps take part.
+__device__ __forceinline__ bool unit_rows(const QMat &m, int k, const DecSmem &sm, Ring &rg, int *err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t w0 = threadIdx.x == 0 ? gtimer() : 0;
+    if (cons_or(!ring_wait(sm, rg, err))) return false;
+    if (threadIdx.x == 0) s_ring_wait += gtimer() - w0;
+    const uint8_t *slot = sm.ring + (size_t)(rg.u % rg.nslots) * rg.slot_bytes;
+    if (k >= kCons) {
+        for (int i = warp; i < k; i += kCons) {
+            double a = dot_tile(m.type, slot + (size_t)i * m.tile_bytes, m.nb, sm, 0, m.nb, lane);
+            a += __shfl_xor_sync(kFull, a, 1);
+            a += __shfl_xor_sync(kFull, a, 2);
+            if ((lane & 3) == 0) sm.rows[i * 8 + (lane >> 2)] = (float)a;
+        }
+    } else {
+        const int parts = kCons / k;
+        const int tile = warp / parts, part = warp % parts;
+        double a = 0.0;
+        if (tile < k) {
+            const int b0 = m.nb * part / parts, b1 = m.nb * (part + 1) / parts;
+            a = dot_tile(m.type, slot + (size_t)tile * m.tile_bytes, m.nb, sm, b0, b1, lane);
+        }
+        a += __shfl_xor_sync(kFull, a, 1);
+        a += __shfl_xor_sync(kFull, a, 2);
+        if ((lane & 3) == 0) sm.part[warp * 8 + (lane >> 2)] = a;
+        cons_sync();
+        if (threadIdx.x < k * 8) {
+            const int t = threadIdx.x >> 3, r = threadIdx.x & 7;
+            double s = 0.0;
+            for (int p = 0; p < parts; ++p) s += sm.part[(t * parts + p) * 8 + r];
+            sm.rows[threadIdx.x] = (float)s;
+        }
+    }
+    ring_release(sm, rg);
+    cons_sync();
+    return true;
+}
+
+// ---------------------------------------------------------------- tags --
+
+__device__ __forceinline__ uint32_t tag_of(uint32_t epoch, int layers, int l, int ph) {
+    // ph: 0 QKV, 1 attention, 2 output projection, 3 gate/up, 4 down; l = -1: the embedding
+    return epoch * (uint32_t)(8 * (layers + 1)) + (uint32_t)(8 * (l + 1) + ph) + 1u;
+}
+
+enum { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4 };
+
+// ------------------------------------------------------------ producer --
+
+__device__ __forceinline__ bool prod_unit(const DecSmem &sm, int nslots, int slot_bytes, unsigned &u, const uint8_t *src,
+                                          unsigned bytes, int *err) {
+    const int slot = u % nslots;
+    const unsigned parity = ((u / nslots) & 1) ^ 1;
+    if (!mbar_try_wait(sm.empty + slot, parity)) {
+        const uint64_t t0 = gtimer();
+        while (!mbar_try_wait(sm.empty + slot, parity)) {
+            if (read_err(err)) return false;
+            if (gtimer() - t0 > kWaitNs) {
+                atomicExch(err, DEV_RING_TIMEOUT);
+                return false;
+            }
+        }
+    }
+    mbar_expect_tx(sm.full + slot, bytes);
+    bulk_g2s(sm.ring + (size_t)slot * slot_bytes, src, bytes, sm.full + slot);
+    u++;
+    return true;
+}
+
+__device__ __forceinline__ bool prod_share(const DecSmem &sm, int nslots, int slot_bytes, unsigned &u, const QMat &m,
+                                           const Share &s, int *err) {
+    for (int t = s.a; t < s.b; t += s.per) {
+        const int k = min(s.per, s.b - t);
+        if (!prod_unit(sm, nslots, slot_bytes, u, m.tiles + (size_t)t * m.tile_bytes, (unsigned)(k * m.tile_bytes), err))
+            return false;
+    }
+    return true;
+}
+
+// The producer's stream: the same order as the consumers' phases.
+__device__ void producer(const DecParams &dm, const DecSmem &sm, int nslots, int slot_bytes, int ntok) {
+    if ((threadIdx.x & 31) != 0) return;
+    const int cta = blockIdx.x, ncta = gridDim.x;
+    unsigned u = 0;
+    bool ok = true;
+    for (int i = 0; i < ntok && ok; ++i) {
+        for (int l = 0; l < dm.layers && ok; ++l) {
+            const Layer &L = dm.layer[l];
+            const int nq = L.q.rows >> 3, nk = L.k.rows >> 3;
+            // QKV: one share over the concatenated tile index space
+            const int T = nq + nk + (L.v.rows >> 3);
+            const int P = min(ncta, T);
+            if (cta < P) {
+                const int a = (int)((int64_t)T * cta / P), b = (int)((int64_t)T * (cta + 1) / P);
+                for (int t = a; t < b && ok; ++t) {
+                    const QMat &m = t < nq ? L.q : t < nq + nk ? L.k : L.v;
+                    const int lt = t < nq ? t : t < nq + nk ? t - nq : t - nq - nk;
+                    ok = prod_unit(sm, nslots, slot_bytes, u, m.tiles + (size_t)lt * m.tile_bytes,
+                                   (unsigned)m.tile_bytes, dm.err);
+                }
+            }
+            if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.o, share(L.o, cta, ncta, slot_bytes), dm.err);
+            if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.gate, share(L.gate, cta, ncta, slot_bytes), dm.err);
+            if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.up, share(L.up, cta, ncta, slot_bytes), dm.err);
+            if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.down, share(L.down, cta, ncta, slot_bytes), dm.err);
+        }
+        if (ok) ok = prod_share(sm, nslots, slot_bytes, u, dm.head, share(dm.head, cta, ncta, slot_bytes), dm.err);
+    }
+    // drain: wait (bounded) for the copies still in flight before the CTA may exit
+    for (unsigned v = u > (unsigned)nslots ? u - nslots : 0; v < u; ++v) {
+        const int slot = v % nslots;
+        const unsigned parity = (v / nslots) & 1;
+        const uint64_t t0 = gtimer();
+        while (!mbar_try_wait(sm.full + slot, parity))
+            if (gtimer() - t0 > kWaitNs) break;
+    }
+}
+
+// -------------------------------------------------------------- phases --
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+struct Tok {
+    int pos, step, tok;
+    uint32_t epoch;
+    Trace tr;  // this token's timeline (first token of a launch only)
+};
+
+// K1: RMSNorm + QKV + bias + RoPE + KV append (kernels_fused.go:47-73).
+__device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
+    const Layer &L = dm.layer[l];
+    const int cta = blockIdx.x, ncta = gridDim.x;
+    const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, T = nq + nk + (L.v.rows >> 3);
+    const int P = min(ncta, T);
+    if (cta >= P) return true;
+    const int E = dm.embd, ev = l * 5 + PH_QKV;
+    tk.tr.stamp(ev, 0);
+    const uint32_t tag_in = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
+    const int a = (int)((int64_t)T * cta / P), b = (int)((int64_t)T * (cta + 1) / P);
+    const int hp = dm.head_dim >> 1;
+    NormW nw;
+    nw.load(L.attn_norm, E);
+    // the epilogue's inputs that do not depend on the token's activations
+    for (int i = threadIdx.x; i < (b - a) * 8; i += kConsThreads) {
+        const int t = a + (i >> 3), r = i & 7;
+        const int seg = t < nq ? 0 : t < nq + nk ? 1 : 2;
+        const int row = (seg == 0 ? t : seg == 1 ? t - nq : t - nq - nk) * 8 + r;
+        const float *bias = seg == 0 ? L.bq : seg == 1 ? L.bk : L.bv;
+        sm.pre[3 * i] = bias ? __ldg(bias + row) : 0.f;
+        float2 cs = make_float2(1.f, 0.f);
+        if (seg < 2) cs = __ldg(reinterpret_cast<const float2 *>(dm.rope_cs) + (size_t)tk.pos * hp + ((row % dm.head_dim) >> 1));
+        sm.pre[3 * i + 1] = cs.x, sm.pre[3 * i + 2] = cs.y;
+    }
+    if (l == 0) {
+        for (int e = threadIdx.x; e < E; e += kConsThreads) {
+            const QMat &m = dm.embed;
+            const uint8_t *t = m.tiles + (size_t)(tk.tok >> 3) * m.tile_bytes;
+            const int r = tk.tok & 7, b = e >> 5, j = e & 31, qb = m.type == 8 ? 32 : 16;
+            const float d = __half2float(reinterpret_cast<const __half *>(t + (size_t)m.nb * 8 * qb)[b * 8 + r]);
+            const uint8_t *qs = t + ((size_t)b * 8 + r) * qb;
+            float v;
+            if (m.type == 8) v = d * (float)(int8_t)qs[j];
+            else v = d * (float)(((j < 16) ? (qs[j & 15] & 15) : (qs[j & 15] >> 4)) - 8);
+            sm.xs[e] = v;
+        }
+        cons_sync();
+    } else {
+        if (cons_or(!poll_vec(dm.ll_x, E, tag_in, sm.xs, dm.err))) return false;
+    }
+    tk.tr.stamp(ev, 1);
+    const bool q8 = L.q.type == 8 || L.k.type == 8 || L.v.type == 8;
+    norm_stage(dm, nw, sm, q8);
+    const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
+    for (int t = a; t < b; ++t) {
+        const int seg = t < nq ? 0 : t < nq + nk ? 1 : 2;
+        const QMat &m = seg == 0 ? L.q : seg == 1 ? L.k : L.v;
+        const int lt = seg == 0 ? t : seg == 1 ? t - nq : t - nq - nk;
+        if (!unit_rows(m, 1, sm, rg, dm.err)) return false;
+        if (threadIdx.x < 8) {
+            const int r = threadIdx.x, row = lt * 8 + r;
+            const float *pre = sm.pre + 3 * ((t - a) * 8);
+            const bool has_bias = (seg == 0 ? L.bq : seg == 1 ? L.bk : L.bv) != nullptr;
+            float v = sm.rows[r];
+            if (has_bias) v = __fadd_rn(v, pre[3 * r]);
+            if (seg < 2) {
+                float o = sm.rows[r ^ 1];
+                if (has_bias) o = __fadd_rn(o, pre[3 * (r ^ 1)]);
+                const float2 cs = make_float2(pre[3 * r + 1], pre[3 * r + 2]);
+                if ((r & 1) == 0) v = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(o, cs.y));
+                else v = __fadd_rn(__fmul_rn(o, cs.y), __fmul_rn(v, cs.x));
+            }
+            if (seg == 0) {
+                ll_put(dm.ll_q + row, v, tag);
+            } else if (seg == 1) {
+                L.kv[(size_t)tk.pos * dm.kvd + row] = v;
+                ll_put(dm.ll_k + row, v, tag);
+            } else {
+                L.kv[((size_t)dm.ctx + tk.pos) * dm.kvd + row] = v;
+                ll_put(dm.ll_v + row, v, tag);
+            }
+        }
+        cons_sync();
+    }
+    tk.tr.stamp(ev, 2);
+    return true;
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
+
+// K2: attention of the token (n = pos + 1 positions) for item (head,
+// chunk of kAttnChunk positions): scores, the chunk's max and sum of exp, the
+// exp-weighted V sum (kernels_fused.go:82-146).  The chunk's cached K and V
+// rows do not depend on this token, so they are copied into shared memory
+// (cp.async) before the item waits for the token's q, k, v.  With one chunk
+// the item writes the head's output; otherwise its partial, chunk-major
+// (ll_pv[c][h][d], ll_ml[c][h][{max, sum}]), for the output projection to
+// merge.  Dot products and sums are accumulated in double.
+template <int HD>
+__device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, int nch, const DecSmem &sm) {
+    constexpr int KS = HD + 16;  // shared row stride: conflict-free 4-threads-per-row reads
+    constexpr int V4 = HD / 4;
+    const int grp = dm.heads / dm.kv_heads;
+    const int h = item / nch, c = item % nch, kvh = h / grp;
+    const int n = tk.pos + 1;
+    const Layer &L = dm.layer[l];
+    const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
+    const uint32_t otag = tag_of(tk.epoch, dm.layers, l, PH_ATT);
+    float *qh = sm.att, *kc = sm.att + HD, *vc = sm.att + 2 * HD, *e = sm.att + 3 * HD;
+    double *part = reinterpret_cast<double *>(sm.att + 3 * HD + kAttnChunk);  // kConsThreads x 4 doubles
+    float *ks = sm.kvs, *vs = sm.kvs + kAttnChunk * KS;
+    const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
+    const bool has_cur = p0 + cnt == n;
+    const int nhist = has_cur ? cnt - 1 : cnt;
+    const int ev = l * 5 + PH_ATT;
+    tk.tr.stamp(ev, 0);
+    for (int i = threadIdx.x; i < nhist * V4; i += kConsThreads) {
+        const int p = i / V4, d4 = i % V4;
+        const size_t row = (size_t)(p0 + p) * dm.kvd + kvh * HD + d4 * 4;
+        cp_async16(ks + p * KS + d4 * 4, L.kv + row);
+        cp_async16(vs + p * KS + d4 * 4, L.kv + (size_t)dm.ctx * dm.kvd + row);
+    }
+    const bool ok = poll_two(dm.ll_q + h * HD, HD, tag, qh, has_cur ? dm.ll_k + kvh * HD : nullptr, has_cur ? HD : 0,
+                             tag, kc, dm.err) &&
+                    (!has_cur || poll_vec(dm.ll_v + kvh * HD, HD, tag, vc, dm.err));
+    cp_async_wait_all();
+    if (cons_or(!ok)) return false;
+    tk.tr.stamp(ev, 1);
+    if (has_cur)
+        for (int i = threadIdx.x; i < HD; i += kConsThreads) ks[nhist * KS + i] = kc[i], vs[nhist * KS + i] = vc[i];
+    cons_sync();
+    // scores: 4 threads per position; thread sub reads float4s sub, sub + 4, ...
+    const int p = threadIdx.x >> 2, sub = threadIdx.x & 3;
+    float s = -FLT_MAX;
+    {
+        double ps0 = 0.0, ps1 = 0.0;
+        if (p < cnt) {
+#pragma unroll
+            for (int j = 0; j < HD / 16; ++j) {
+                const int d = 4 * (sub + 4 * j);
+                const float4 k4 = *reinterpret_cast<const float4 *>(ks + p * KS + d);
+                const float4 q4 = *reinterpret_cast<const float4 *>(qh + d);
+                ps0 = fma((double)q4.x, (double)k4.x, ps0);
+                ps1 = fma((double)q4.y, (double)k4.y, ps1);
+                ps0 = fma((double)q4.z, (double)k4.z, ps0);
+                ps1 = fma((double)q4.w, (double)k4.w, ps1);
+            }
+        }
+        double ps = ps0 + ps1;
+        ps += __shfl_xor_sync(kFull, ps, 1);
+        ps += __shfl_xor_sync(kFull, ps, 2);
+        if (p < cnt) s = __fmul_rn((float)ps, dm.scale);
+    }
+    const float mx = cons_max(s, sm.red);
+    if (p < cnt && sub == 0) e[p] = (float)exp((double)__fsub_rn(s, mx));
+    cons_sync();
+    constexpr int G = kConsThreads / V4;
+    const int d4 = threadIdx.x % V4, g = threadIdx.x / V4;
+    double o0 = 0, o1 = 0, o2 = 0, o3 = 0;
+#pragma unroll
+    for (int k = 0; k < kAttnChunk / G; ++k) {
+        const int pp = g + k * G;
+        if (pp < cnt) {
+            const double w = e[pp];
+            const float4 v4 = *reinterpret_cast<const float4 *>(vs + pp * KS + d4 * 4);
+            o0 = fma(w, (double)v4.x, o0);
+            o1 = fma(w, (double)v4.y, o1);
+            o2 = fma(w, (double)v4.z, o2);
+            o3 = fma(w, (double)v4.w, o3);
+        }
+    }
+    part[threadIdx.x * 4 + 0] = o0, part[threadIdx.x * 4 + 1] = o1;
+    part[threadIdx.x * 4 + 2] = o2, part[threadIdx.x * 4 + 3] = o3;
+    cons_sync();
+    if (threadIdx.x < V4) {
+        double t4[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int k = 0; k < G; ++k)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) t4[j] += part[(threadIdx.x + k * V4) * 4 + j];
+        double lsum = 0.0;
+        for (int pp = 0; pp < cnt; ++pp) lsum += e[pp];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int d = threadIdx.x * 4 + j;
+            if (nch == 1) ll_put(dm.ll_att + h * HD + d, (float)(t4[j] / lsum), otag);
+            else ll_put(dm.ll_pv + ((size_t)c * dm.heads + h) * HD + d, (float)t4[j], otag);
+        }
+        if (nch > 1 && threadIdx.x == 0) {
+            ll_put(dm.ll_ml + ((size_t)c * dm.heads + h) * 2, mx, otag);
+            ll_put(dm.ll_ml + ((size_t)c * dm.heads + h) * 2 + 1, (float)lsum, otag);
+        }
+    }
+    cons_sync();
+    tk.tr.stamp(ev, 2);
+    return true;
+}
+
+__device__ bool ph_attn(const DecParams &dm, int l, const Tok &tk, int item, int nch, const DecSmem &sm) {
+    return dm.head_dim == 128 ? ph_attn_t<128>(dm, l, tk, item, nch, sm) : ph_attn_t<64>(dm, l, tk, item, nch, sm);
+}
+
+// The merged attention of all heads into sm.xs (E floats), and the
+// residual rows [r0, r0 + nr) into sm.gate: with several chunks, the chunks'
+// partials are merged (kernels_fused.go:150-170) in groups of up to 8, in
+// double.
+__device__ bool gather_att(const DecParams &dm, int l, const Tok &tk, int nch, const DecSmem &sm, int r0, int nr,
+                           uint32_t xtag) {
+    const int HD = dm.head_dim, E = dm.embd, H = dm.heads;
+    const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_ATT);
+    if (nch == 1) return !cons_or(!poll_two(dm.ll_att, E, tag, sm.xs, dm.ll_x + r0, nr, xtag, sm.gate, dm.err));
+    // running merge over groups of up to 8 chunks: per head the max M and the
+    // sum L of the chunks' exp sums, rescaled; per element the weighted sum O
+    double accO[4];
+    const int per = (E + kConsThreads - 1) / kConsThreads;  // <= 4 (embd <= 1024)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) accO[k] = 0;
+    double *hM = reinterpret_cast<double *>(sm.merge + 8 * E + 16 * H);  // [H] running max
+    double *hL = hM + H;                                                  // [H] running sum
+    double *fc = hL + H;                                                  // [8][H] chunk factors, then [H] rescale
+    for (int i = threadIdx.x; i < H; i += kConsThreads) hM[i] = -1e300, hL[i] = 0;
+    for (int c0 = 0; c0 < nch; c0 += 8) {
+        const int gn = min(8, nch - c0);
+        float *pv = sm.merge, *ml = sm.merge + 8 * E;
+        const bool first = c0 == 0;
+        const Seg sg[3] = {{dm.ll_pv + (size_t)c0 * H * HD, gn * E, tag, pv},
+                           {dm.ll_ml + (size_t)c0 * H * 2, gn * H * 2, tag, ml},
+                           {dm.ll_x + r0, first ? nr : 0, xtag, sm.gate}};
+        if (cons_or(!poll_segs(sg, dm.err))) return false;
+        for (int h = threadIdx.x; h < H; h += kConsThreads) {
+            double M = hM[h];
+            for (int c = 0; c < gn; ++c) M = fmax(M, (double)ml[(c * H + h) * 2]);
+            const double rs = exp(hM[h] - M);
+            double Ls = hL[h] * rs;
+            for (int c = 0; c < gn; ++c) {
+                const double f = exp((double)ml[(c * H + h) * 2] - M);
+                fc[c * H + h] = f;
+                Ls = fma(f, (double)ml[(c * H + h) * 2 + 1], Ls);
+            }
+            fc[8 * H + h] = rs;
+            hM[h] = M, hL[h] = Ls;
+        }
+        cons_sync();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = threadIdx.x + k * kConsThreads;
+            if (k >= per || i >= E) continue;
+            const int h = i / HD;
+            double O = accO[k] * fc[8 * H + h];
+            for (int c = 0; c < gn; ++c) O = fma(fc[c * H + h], (double)pv[c * E + i], O);
+            accO[k] = O;
+        }
+        cons_sync();
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = threadIdx.x + k * kConsThreads;
+        if (k < per && i < E) sm.xs[i] = (float)(accO[k] / hL[i / HD]);
+    }
+    cons_sync();
+    return true;
+}
+
+// K3: x += Wo att (cpu.go:336-339).
+__device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, int nch, const DecSmem &sm, Ring &rg) {
+    const Layer &L = dm.layer[l];
+    const Share s = share(L.o, blockIdx.x, gridDim.x, rg.slot_bytes);
+    if (s.b <= s.a) return true;
+    const uint32_t tin = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
+    const int ev = l * 5 + PH_O;
+    tk.tr.stamp(ev, 0);
+    if (!gather_att(dm, l, tk, nch, sm, s.a * 8, (s.b - s.a) * 8, tin)) return false;
+    tk.tr.stamp(ev, 1);
+    stage_vector(sm.xs, dm.embd, sm, L.o.type == 8);
+    cons_sync();
+    const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_O);
+    for (int t = s.a; t < s.b; t += s.per) {
+        const int k = min(s.per, s.b - t);
+        if (!unit_rows(L.o, k, sm, rg, dm.err)) return false;
+        if (threadIdx.x < k * 8) {
+            const int row = t * 8 + threadIdx.x;
+            ll_put(dm.ll_x + row, __fadd_rn(sm.gate[row - s.a * 8], sm.rows[threadIdx.x]), tag);
+        }
+        cons_sync();
+    }
+    tk.tr.stamp(ev, 2);
+    return true;
+}
+
+// K4: RMSNorm + gate/up + SwiGLU (cpu.go:340-346).
+__device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
+    const Layer &L = dm.layer[l];
+    const Share sg = share(L.gate, blockIdx.x, gridDim.x, rg.slot_bytes);
+    const Share su = share(L.up, blockIdx.x, gridDim.x, rg.slot_bytes);
+    if (sg.b <= sg.a) return true;
+    const int E = dm.embd, ev = l * 5 + PH_GU;
+    tk.tr.stamp(ev, 0);
+    const uint32_t tin = tag_of(tk.epoch, dm.layers, l, PH_O);
+    NormW nw;
+    nw.load(L.ffn_norm, E);
+    if (cons_or(!poll_vec(dm.ll_x, E, tin, sm.xs, dm.err))) return false;
+    tk.tr.stamp(ev, 1);
+    norm_stage(dm, nw, sm, L.gate.type == 8 || L.up.type == 8);
+    for (int t = sg.a; t < sg.b; t += sg.per) {
+        const int k = min(sg.per, sg.b - t);
+        if (!unit_rows(L.gate, k, sm, rg, dm.err)) return false;
+        if (threadIdx.x < k * 8) sm.gate[(t - sg.a) * 8 + threadIdx.x] = sm.rows[threadIdx.x];
+        cons_sync();
+    }
+    const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_GU);
+    for (int t = su.a; t < su.b; t += su.per) {
+        const int k = min(su.per, su.b - t);
+        if (!unit_rows(L.up, k, sm, rg, dm.err)) return false;
+        if (threadIdx.x < k * 8) {
+            const int row = t * 8 + threadIdx.x;
+            const float g = sm.gate[(t - su.a) * 8 + threadIdx.x], u = sm.rows[threadIdx.x];
+            if (row < dm.ff) {
+                const float den = __fadd_rn(1.f, (float)exp(-(double)g));
+                ll_put(dm.ll_act + row, __fmul_rn(__fdiv_rn(g, den), u), tag);
+            }
+        }
+        cons_sync();
+    }
+    tk.tr.stamp(ev, 2);
+    return true;
+}
+
+// K5: x += Wdown act (cpu.go:347-350).
+__device__ bool ph_down(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
+    const Layer &L = dm.layer[l];
+    const Share s = share(L.down, blockIdx.x, gridDim.x, rg.slot_bytes);
+    if (s.b <= s.a) return true;
+    const int F = dm.ff;
+    const uint32_t tact = tag_of(tk.epoch, dm.layers, l, PH_GU), tin = tag_of(tk.epoch, dm.layers, l, PH_O);
+    const int ev = l * 5 + PH_DOWN;
+    tk.tr.stamp(ev, 0);
+    if (cons_or(!poll_two(dm.ll_act, F, tact, sm.xs, dm.ll_x + s.a * 8, (s.b - s.a) * 8, tin, sm.gate, dm.err)))
+        return false;
+    tk.tr.stamp(ev, 1);
+    stage_vector(sm.xs, F, sm, L.down.type == 8);
+    cons_sync();
+    const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_DOWN);
+    for (int t = s.a; t < s.b; t += s.per) {
+        const int k = min(s.per, s.b - t);
+        if (!unit_rows(L.down, k, sm, rg, dm.err)) return false;
+        if (threadIdx.x < k * 8) {
+            const int row = t * 8 + threadIdx.x;
+            ll_put(dm.ll_x + row, __fadd_rn(sm.gate[row - s.a * 8], sm.rows[threadIdx.x]), tag);
+        }
+        cons_sync();
+    }
+    tk.tr.stamp(ev, 2);
+    return true;
+}
+
+// The head: RMSNorm(output_norm), logits, this CTA's argmax partial.
+__device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, Ring &rg) {
+    const Share s = share(dm.head, blockIdx.x, gridDim.x, rg.slot_bytes);
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    const int ev = dm.layers * 5;
+    tk.tr.stamp(ev, 0);
+    if (s.b > s.a) {
+        const int E = dm.embd;
+        const uint32_t tin = tag_of(tk.epoch, dm.layers, dm.layers - 1, PH_DOWN);
+        NormW nw;
+        nw.load(dm.out_norm, E);
+        if (cons_or(!poll_vec(dm.ll_x, E, tin, sm.xs, dm.err))) return false;
+        tk.tr.stamp(ev, 1);
+        norm_stage(dm, nw, sm, dm.head.type == 8);
+        for (int t = s.a; t < s.b; t += s.per) {
+            const int k = min(s.per, s.b - t);
+            if (!unit_rows(dm.head, k, sm, rg, dm.err)) return false;
+            if (threadIdx.x < k * 8) {
+                const int row = t * 8 + threadIdx.x;
+                const float v = sm.rows[threadIdx.x];
+                if (row < dm.vocab) {
+                    dm.logits[row] = v;
+                    if (better(v, row, bv, bi)) bv = v, bi = row;
+                }
+            }
+            cons_sync();
+        }
+    }
+    // CTA argmax over the threads that saw rows (all 8 warps reduce; idle lanes hold the identity)
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bv, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (better(ov, oi, bv, bi)) bv = ov, bi = oi;
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) sm.red[w] = bv, sm.red[kCons + w] = __int_as_float(bi);
+    cons_sync();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < kCons; ++k) {
+            const float v = sm.red[k];
+            const int i = __float_as_int(sm.red[kCons + k]);
+            if (better(v, i, bv, bi)) bv = v, bi = i;
+        }
+        dm.am_part[blockIdx.x] = make_float2(bv, __int_as_float(bi));
+    }
+    tk.tr.stamp(ev, 2);
+    return true;
+}
+
+__device__ int final_argmax(const DecParams &dm, const DecSmem &sm) {
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += kConsThreads) {
+        const float2 p = __ldcg(dm.am_part + i);
+        if (better(p.x, __float_as_int(p.y), bv, bi)) bv = p.x, bi = __float_as_int(p.y);
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bv, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (better(ov, oi, bv, bi)) bv = ov, bi = oi;
+    }
+    const int w = threadIdx.x >> 5;
+    cons_sync();
+    if ((threadIdx.x & 31) == 0) sm.red[w] = bv, sm.red[kCons + w] = __int_as_float(bi);
+    cons_sync();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < kCons; ++k) {
+            const float v = sm.red[k];
+            const int i = __float_as_int(sm.red[kCons + k]);
+            if (better(v, i, bv, bi)) bv = v, bi = i;
+        }
+        sm.red[2 * kCons] = __int_as_float(bi == 0x7fffffff ? 0 : bi);
+    }
+    cons_sync();
+    return __float_as_int(sm.red[2 * kCons]);
+}
+
+__global__ void __launch_bounds__(kDecThreads, 1)
+    k_decode2(const __grid_constant__ DecParams dm, GridBarrier *bar, int ntok, int nslots, int slot_bytes) {
+    extern __shared__ __align__(128) uint8_t dsm[];
+    DecSmem sm;
+    {
+        const DecLayout lo =
+            dec_layout(nslots, slot_bytes, dm.embd, dm.ff, dm.head_dim, dm.heads, dm.dec_gate_rows, dm.dec_qkv_rows);
+        sm.ring = dsm + lo.ring;
+        sm.full = reinterpret_cast<uint64_t *>(dsm + lo.full);
+        sm.empty = reinterpret_cast<uint64_t *>(dsm + lo.empty);
+        sm.xv = reinterpret_cast<float *>(dsm + lo.xv);
+        sm.xq8 = reinterpret_cast<float *>(dsm + lo.xq8);
+        sm.xs = reinterpret_cast<float *>(dsm + lo.xs);
+        sm.part = reinterpret_cast<double *>(dsm + lo.part);
+        sm.rows = reinterpret_cast<float *>(dsm + lo.rows);
+        sm.gate = reinterpret_cast<float *>(dsm + lo.gate);
+        sm.red = reinterpret_cast<float *>(dsm + lo.red);
+        sm.att = reinterpret_cast<float *>(dsm + lo.att);
+        sm.merge = reinterpret_cast<float *>(dsm + lo.merge);
+        sm.pre = reinterpret_cast<float *>(dsm + lo.pre);
+        sm.kvs = reinterpret_cast<float *>(dsm + lo.kvs);
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nslots; ++i) mbar_init(sm.full + i, 1), mbar_init(sm.empty + i, kCons);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x >= kConsThreads) {
+        producer(dm, sm, nslots, slot_bytes, ntok);
+        return;
+    }
+    Ring rg{nslots, slot_bytes, 0u};
+    Tok tk;
+    tk.pos = (int)__ldcg(dm.state), tk.step = (int)__ldcg(dm.state + 1);
+    tk.tok = __ldcg(dm.tokens + tk.step);
+    tk.epoch = __ldcg(dm.ll_epoch);
+    for (int i = 0; i < ntok; ++i) {
+        if (tk.pos >= dm.ctx) {
+            if (threadIdx.x == 0) atomicExch(dm.err, DEV_CONTEXT_FULL);
+            return;
+        }
+        const int nch = (tk.pos + 1 + kAttnChunk - 1) / kAttnChunk;
+        tk.tr.p = (dm.trace && i == 0) ? dm.trace + (size_t)blockIdx.x * dm.trace_events * 4 : nullptr;
+        if (threadIdx.x == 0) s_ring_wait = 0;
+        if (blockIdx.x == 0) {  // the embedding row is the residual of layer 0
+            for (int e = threadIdx.x; e < dm.embd; e += kConsThreads) {
+                const QMat &m = dm.embed;
+                const uint8_t *t = m.tiles + (size_t)(tk.tok >> 3) * m.tile_bytes;
+                const int r = tk.tok & 7, b = e >> 5, j = e & 31, qb = m.type == 8 ? 32 : 16;
+                const float d = __half2float(reinterpret_cast<const __half *>(t + (size_t)m.nb * 8 * qb)[b * 8 + r]);
+                const uint8_t *qs = t + ((size_t)b * 8 + r) * qb;
+                const float v = m.type == 8 ? d * (float)(int8_t)qs[j]
+                                            : d * (float)(((j < 16) ? (qs[j & 15] & 15) : (qs[j & 15] >> 4)) - 8);
+                ll_put(dm.ll_x + e, v, tag_of(tk.epoch, dm.layers, -1, PH_DOWN));
+            }
+        }
+        for (int l = 0; l < dm.layers; ++l) {
+            if (!ph_qkv(dm, l, tk, sm, rg)) return;
+            for (int item = blockIdx.x; item < dm.heads * nch; item += gridDim.x)
+                if (!ph_attn(dm, l, tk, item, nch, sm)) return;
+            if (!ph_o(dm, l, tk, nch, sm, rg)) return;
+            if (!ph_gu(dm, l, tk, sm, rg)) return;
+            if (!ph_down(dm, l, tk, sm, rg)) return;
+        }
+        if (!ph_head(dm, tk, sm, rg)) return;
+        tk.tr.stamp(dm.layers * 5 + 1, 0);
+        if (!grid_sync_cons(bar, dm.err)) return;
+        tk.tr.stamp(dm.layers * 5 + 1, 2);
+        tk.tok = final_argmax(dm, sm);
+        tk.pos++, tk.step++, tk.epoch++;
+        if (blockIdx.x == 0 && threadIdx.x == 0) dm.tokens[tk.step] = tk.tok;
+        // the partials are read before any CTA writes the next token's (its head comes after every phase)
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        dm.state[0] = tk.pos;
+        dm.state[1] = tk.step;
+        *dm.ll_epoch = tk.epoch;
+    }
+}
+
+}  // namespace
+
+DecConfig decode_config(const Shapes &s, int max_tile_bytes, int gate_rows, int qkv_rows) {
+    DecConfig c{};
+    const int budget = 232448 - 8192;  // the opt-in maximum per block, less the rest of the layout and margin
+    DecLayout base = dec_layout(0, 0, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows);
+    const int ring = budget - (int)base.total;
+    int slot = max(max_tile_bytes, ring / 9);
+    slot = (slot + 127) / 128 * 128;
+    c.slot_bytes = slot;
+    c.nslots = min(32, ring / slot);
+    c.smem = dec_layout(c.nslots, c.slot_bytes, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows).total;
+    c.threads = kDecThreads;
+    return c;
+}
+
+cudaError_t launch_decode2(const DecParams &dm, const DecConfig &c, GridBarrier *bar, int ntok, int ctas,
+                           cudaStream_t st) {
+    cudaError_t e = cudaFuncSetAttribute(k_decode2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(c.threads);
+    cfg.dynamicSmemBytes = c.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_decode2, dm, bar, ntok, c.nslots, c.slot_bytes);
+}
+
+int decode2_ctas_per_sm(const DecConfig &c) {
+    int n = 0;
+    cudaFuncSetAttribute(k_decode2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode2, c.threads, c.smem);
+    return n;
+}
+
+}  // namespace llmb

@@ -49,15 +49,14 @@ struct Layer {
     float *kv = nullptr;  // [2][ctx][kvd]: K at 0, V at ctx * kvd (fused.go:221, kernels_fused.go:440-445)
 };
 
-// Everything a kernel needs, resident in device memory (one per model).
-struct DevModel {
+// What the kernels need besides the per-layer descriptors.
+struct ModelHeader {
     int embd, ff, heads, kv_heads, head_dim, kvd, vocab, ctx, layers;
     float eps, scale;  // RMSNorm epsilon; 1/sqrt(head_dim) (cpu.go:304)
     int rope_neox;
     QMat embed, head;  // token_embd (the gather) and the output matrix (token_embd when tied)
     const float *out_norm;
     const float *rope_cs;  // [ctx][head_dim/2][2] cos, sin (gpu.go:524-534)
-    Layer layer[kMaxLayers];
 
     // activations
     float *x;       // residual stream [kMaxPrefill][embd]
@@ -76,6 +75,67 @@ struct DevModel {
     float2 *am_part;   // argmax partials per CTA (value, index as float bits)
     uint32_t *am_count;// arrival counter of the head kernel's CTAs
     int *err;          // device error word (0 = none)
+
+    // the persistent decode kernel's tagged activations ({f32 value, u32 tag})
+    uint64_t *ll_x, *ll_q, *ll_k, *ll_v, *ll_att, *ll_act, *ll_pv, *ll_ml;
+    uint32_t *ll_epoch;  // tokens decoded so far by the persistent kernel (makes tags unique across calls)
+    int dec_gate_rows;   // gate rows of the largest gate/up share of a CTA
+    int dec_qkv_rows;    // rows of the largest QKV share of a CTA
+    // optional phase timeline of the persistent decode kernel (null: off):
+    // trace[(cta * trace_events + event) * 4 + {0, 1, 2}] = globaltimer ns at
+    // the phase's entry, when its input was ready, at its exit, and + 3 the
+    // ns it waited for weight slots; events are
+    // 5 per layer (QKV, attention, output, gate/up, down), then head, then
+    // the token's grid barrier.  Recorded for the first token of a launch.
+    uint64_t *trace;
+    int trace_events;
 };
+
+
+// Everything a kernel needs (header + layers).  DevModel lives in device
+// memory for the per-phase kernels; DecParams is the persistent decode
+// kernel's __grid_constant__ parameter (constant memory, so the uniform
+// descriptor reads of every phase hit the constant cache, not L1, which the
+// kernel's large shared memory leaves small).
+template <int NL>
+struct ModelDesc : ModelHeader {
+    Layer layer[NL];
+};
+constexpr int kMaxDecLayers = 64;
+using DevModel = ModelDesc<kMaxLayers>;
+using DecParams = ModelDesc<kMaxDecLayers>;
+static_assert(sizeof(DecParams) < 32000, "kernel parameters are limited to 32 KB");
+
+// Shared-memory layout of the persistent decode kernel (byte offsets).
+struct DecLayout {
+    size_t ring, full, empty, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, total;
+};
+
+__host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int embd, int ff, int head_dim, int heads,
+                                                int gate_rows, int qkv_rows) {
+    DecLayout l{};
+    const size_t vec = (size_t)(embd > ff ? embd : ff) * 4;
+    size_t p = 0;
+    l.ring = p, p += (size_t)nslots * slot_bytes;
+    l.full = p, p += 8 * (size_t)nslots;
+    l.empty = p, p += 8 * (size_t)nslots;
+    p = (p + 127) / 128 * 128;
+    l.xv = p, p += vec;
+    l.xq8 = p, p += vec;
+    l.xs = p, p += vec;
+    l.part = p, p += 8 * 64;
+    l.rows = p, p += 4 * 256;
+    l.gate = p, p += 4 * (size_t)gate_rows;
+    p = (p + 15) / 16 * 16;
+    l.red = p, p += 4 * 64;
+    l.att = p, p += 4 * (size_t)(3 * head_dim + 64) + 8 * 4 * 256;
+    p = (p + 15) / 16 * 16;
+    l.merge = p, p += 4 * (size_t)(8 * embd + 8 * 2 * heads) + 8 * (size_t)(2 * heads + 9 * heads) + 16;
+    l.pre = p, p += 4 * (size_t)(3 * qkv_rows);
+    p = (p + 127) / 128 * 128;
+    l.kvs = p, p += 4 * (size_t)(2 * 64 * (head_dim + 16));
+    l.total = (p + 127) / 128 * 128;
+    return l;
+}
 
 }  // namespace llmb

@@ -33,6 +33,7 @@ std::atomic<int64_t> g_decode_batch{8};
 std::atomic<int64_t> g_prefill_batch{kMaxPrefill};
 std::atomic<int64_t> g_memory_budget{0};
 std::atomic<int64_t> g_decode_mode{0};  // 0: persistent kernel, 1: per-phase kernels
+std::atomic<int64_t> g_decode_trace{0}; // 1: record the persistent kernel's phase timeline (read by llmb_peek "trace")
 
 thread_local std::string t_open_error;
 
@@ -66,6 +67,8 @@ struct Model {
     int pm = kMaxPrefill;  // tokens per prefill chunk
     int layers_run = 0;    // GPU.Layers (0: all)
     int persistent_ctas = 0;
+    DecConfig dec{};
+    std::unique_ptr<DecParams> dp;  // the decode kernel's parameter block (header + layers)
     int32_t *h_tokens = nullptr;  // pinned: prompt upload and sampled-token read-back
     uint32_t *h_state = nullptr;
     int *h_err = nullptr;
@@ -274,8 +277,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, m.device));
     s.head_ctas = std::max(1, std::min(nsm * 2, (s.head_tiles + kWarps - 1) / kWarps));
     d.smem_vec = smem_vec_floats(s);
-    int per_sm = persistent_ctas_per_sm(s);
-    m.persistent_ctas = nsm * std::max(1, std::min(per_sm, 1));
+    m.persistent_ctas = nsm;
 
     Error err{LLMB_OK, ""};
     Loader ld{m, f, read};
@@ -346,8 +348,47 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     if (!(d.am_count = m.alloc<uint32_t>(4, err))) return err;
     if (!(d.err = m.alloc<int>(4, err))) return err;
     if (!(m.bar = m.alloc<GridBarrier>(sizeof(GridBarrier), err))) return err;
+    // the persistent decode kernel: tagged activations and its ring configuration
+    if (!(d.ll_x = m.alloc<uint64_t>((size_t)E * 8, err))) return err;
+    if (!(d.ll_q = m.alloc<uint64_t>((size_t)E * 8, err))) return err;
+    if (!(d.ll_k = m.alloc<uint64_t>((size_t)kvd * 8, err))) return err;
+    if (!(d.ll_v = m.alloc<uint64_t>((size_t)kvd * 8, err))) return err;
+    if (!(d.ll_att = m.alloc<uint64_t>((size_t)E * 8, err))) return err;
+    if (!(d.ll_act = m.alloc<uint64_t>((size_t)F * 8, err))) return err;
+    if (!(d.ll_pv = m.alloc<uint64_t>((size_t)c.heads * d.nchunk * c.head_dim * 8, err))) return err;
+    if (!(d.ll_ml = m.alloc<uint64_t>((size_t)c.heads * d.nchunk * 2 * 8, err))) return err;
+    if (!(d.ll_epoch = m.alloc<uint32_t>(4, err))) return err;
+    d.trace_events = c.layers * 5 + 2;
+    if (g_decode_trace.load() &&
+        !(d.trace = m.alloc<uint64_t>((size_t)m.persistent_ctas * d.trace_events * 4 * 8, err)))
+        return err;
+    {
+        int max_tile = d.head.tile_bytes;
+        for (int l = 0; l < c.layers; l++) {
+            const Layer &L = d.layer[l];
+            for (const QMat *q : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) max_tile = std::max(max_tile, q->tile_bytes);
+        }
+        const int T = F / 8, P = std::min(m.persistent_ctas, T);
+        d.dec_gate_rows = (T + P - 1) / P * 8;
+        const int Tq = (E + 2 * kvd) / 8, Pq = std::min(m.persistent_ctas, Tq);
+        d.dec_qkv_rows = (Tq + Pq - 1) / Pq * 8;
+        // the output and down shares reuse the gate buffer for their residual rows
+        const int To = E / 8, Po = std::min(m.persistent_ctas, To);
+        d.dec_gate_rows = std::max(d.dec_gate_rows, (To + Po - 1) / Po * 8);
+        if (E > 1024) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports embedding sizes up to 1024"};
+        if (c.head_dim != 64 && c.head_dim != 128)
+            return {LLMB_ERR_CONFIG, "llm: the decode kernel supports head sizes 64 and 128"};
+        m.dec = decode_config(s, max_tile, d.dec_gate_rows, d.dec_qkv_rows);
+        if (c.layers > kMaxDecLayers) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports up to 64 layers"};
+        if (m.dec.nslots < 2 || decode2_ctas_per_sm(m.dec) < 1)
+            return {LLMB_ERR_CONFIG, "llm: the decode kernel does not fit an SM (tiles of " + std::to_string(max_tile) +
+                                         " bytes)"};
+    }
     if (!(m.dm = m.alloc<DevModel>(sizeof(DevModel), err))) return err;
     CUDA_TRY(cudaMemcpyAsync(m.dm, &d, sizeof(DevModel), cudaMemcpyHostToDevice, m.st));
+    m.dp = std::make_unique<DecParams>();
+    static_cast<ModelHeader &>(*m.dp) = static_cast<const ModelHeader &>(d);
+    for (int l = 0; l < c.layers; l++) m.dp->layer[l] = d.layer[l];
     CUDA_TRY(cudaHostAlloc(&m.h_tokens, (size_t)(ctx + 2 * kMaxDecodeBatch + 1) * 4, cudaHostAllocDefault));
     CUDA_TRY(cudaHostAlloc(&m.h_state, 16, cudaHostAllocDefault));
     CUDA_TRY(cudaHostAlloc(&m.h_err, 4, cudaHostAllocDefault));
@@ -366,8 +407,11 @@ Error check_device(Model &m) {
         *m.h_err = 0;
         cudaMemsetAsync(m.hdm.err, 0, 4, m.st);
         cudaStreamSynchronize(m.st);
-        return {LLMB_ERR_DEVICE, e == DEV_BARRIER_TIMEOUT ? "llm: a grid barrier of the decode kernel timed out"
-                                                          : "llm: a token past the context"};
+        const char *what = e == DEV_BARRIER_TIMEOUT ? "a grid barrier of the decode kernel timed out"
+                           : e == DEV_TAG_TIMEOUT   ? "an activation of the decode kernel did not arrive in time"
+                           : e == DEV_RING_TIMEOUT  ? "a weight slot of the decode kernel timed out"
+                                                    : "a token past the context";
+        return {LLMB_ERR_DEVICE, std::string("llm: ") + what};
     }
     return {LLMB_OK, ""};
 }
@@ -412,7 +456,7 @@ Error prefill(Model &m, int n) {
 // cnt decode tokens: the persistent kernel (one launch) or the per-phase kernels.
 Error decode(Model &m, int cnt) {
     if (g_decode_mode.load() == 0) {
-        CUDA_TRY(launch_decode_persistent(m.dm, m.sh, m.bar, cnt, m.persistent_ctas, m.st));
+        CUDA_TRY(launch_decode2(*m.dp, m.dec, m.bar, cnt, m.persistent_ctas, m.st));
         m.stats.dispatches++;
     } else {
         for (int j = 0; j < cnt; j++) {
@@ -585,6 +629,7 @@ Error peek(Model &m, const char *name, float *out, int n) {
     else if (s == "logits") p = d.logits, words = d.vocab;
     else if (s == "state") p = d.state, words = 2;
     else if (s == "tokens") p = d.tokens, words = (size_t)d.ctx + 1;
+    else if (s == "trace" && d.trace) p = d.trace, words = (size_t)m.persistent_ctas * d.trace_events * 4 * 2;
     else if (s.rfind("kvblk.", 0) == 0) {
         int l = -1;
         if (std::sscanf(s.c_str(), "kvblk.%d.", &l) == 1 && l >= 0 && l < d.layers)
@@ -737,6 +782,7 @@ int llmb_set_knob(const char *name, int64_t v) {
     else if (s == "prefill_batch") g_prefill_batch = std::clamp<int64_t>(v, 1, kMaxPrefill);
     else if (s == "memory_budget") g_memory_budget = std::max<int64_t>(v, 0);
     else if (s == "decode_mode") g_decode_mode = v ? 1 : 0;
+    else if (s == "decode_trace") g_decode_trace = v ? 1 : 0;
     else return LLMB_ERR_ARG;
     return LLMB_OK;
 }
@@ -748,6 +794,7 @@ int64_t llmb_get_knob(const char *name) {
     if (s == "prefill_batch") return g_prefill_batch;
     if (s == "memory_budget") return g_memory_budget;
     if (s == "decode_mode") return g_decode_mode;
+    if (s == "decode_trace") return g_decode_trace;
     return -1;
 }
 

@@ -20,9 +20,9 @@
 //     projection reads a finished vector;
 //   - the vocab argmax (first index of the largest logit, cpu.go:387-397)
 //     is fused into the head product: per-CTA partials, then a final pass.
-// Every phase is a device function over work items, called from per-phase
-// kernels (m tokens) and from one persistent cooperative decode kernel that
-// separates the phases with bounded grid barriers.
+// Every phase is a device function over work items; these kernels run m
+// tokens per launch (prefill chunks, and decode with decode_mode 1).  The
+// persistent decode kernel is in decode.cu.
 #include <cuda_fp16.h>
 
 #include <cfloat>
@@ -74,7 +74,8 @@ __device__ __forceinline__ float b2f(uint32_t v, int k) {
 
 // ---------------------------------------------------------------- dot --
 // Each returns, in all 4 lanes of row r = lane / 4, the dot product of tile
-// row r with the vector xs (shared memory, nb * 32 floats).
+// row r with the vector xs (shared memory, nb * 32 floats).  A block's 8-term
+// sum is f32; the sum over blocks is double, rounded once at the end.
 
 // Q4_0: value d * (q - 8); byte j of a block holds element j (low nibble)
 // and j + 16 (high nibble) (cpu.go:164-179).  Lane q owns bytes 4q..4q+3.
@@ -85,7 +86,7 @@ __device__ __forceinline__ float dot_q4_0(const uint8_t *__restrict__ tile, int 
     const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 128) + r;
     const float *xp = xs + 4 * q;
     constexpr float kOff = 8388616.f;  // 2^23 + 8
-    float acc = 0.f;
+    double acc = 0.0;
 #pragma unroll 2
     for (int b = 0; b < nb; ++b) {
         const uint32_t w = __ldg(qw + b * 32);
@@ -101,11 +102,11 @@ __device__ __forceinline__ float dot_q4_0(const uint8_t *__restrict__ tile, int 
         s = fmaf(b2f(hi, 2) - kOff, x1.z, s);
         s = fmaf(b2f(lo, 3) - kOff, x0.w, s);
         s = fmaf(b2f(hi, 3) - kOff, x1.w, s);
-        acc = fmaf(d, s, acc);
+        acc = fma((double)d, (double)s, acc);
     }
     acc += __shfl_xor_sync(kFull, acc, 1);
     acc += __shfl_xor_sync(kFull, acc, 2);
-    return acc;
+    return (float)acc;
 }
 
 // Q4_1: value d * q + m (cpu.go:181-200): sum d * sum(q x) + m * sum(x).
@@ -117,7 +118,7 @@ __device__ __forceinline__ float dot_q4_1(const uint8_t *__restrict__ tile, int 
     const __half *mp = dp + nb * 8;
     const float *xp = xs + 4 * q;
     constexpr float kOff = 8388608.f;  // 2^23
-    float acc = 0.f;
+    double acc = 0.0;
 #pragma unroll 2
     for (int b = 0; b < nb; ++b) {
         const uint32_t w = __ldg(qw + b * 32);
@@ -135,11 +136,11 @@ __device__ __forceinline__ float dot_q4_1(const uint8_t *__restrict__ tile, int 
         s = fmaf(b2f(lo, 3) - kOff, x0.w, s);
         s = fmaf(b2f(hi, 3) - kOff, x1.w, s);
         const float sx = ((x0.x + x0.y) + (x0.z + x0.w)) + ((x1.x + x1.y) + (x1.z + x1.w));
-        acc += fmaf(d, s, mn * sx);
+        acc = fma((double)d, (double)s, fma((double)mn, (double)sx, acc));
     }
     acc += __shfl_xor_sync(kFull, acc, 1);
     acc += __shfl_xor_sync(kFull, acc, 2);
-    return acc;
+    return (float)acc;
 }
 
 // Q8_0: value d * int8 (cpu.go:201-215).  Lane q owns bytes 8q..8q+7.
@@ -150,7 +151,7 @@ __device__ __forceinline__ float dot_q8_0(const uint8_t *__restrict__ tile, int 
     const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 256) + r;
     const float *xp = xs + 8 * q;
     constexpr float kOff = 8388736.f;  // 2^23 + 128: bytes are biased by 128
-    float acc = 0.f;
+    double acc = 0.0;
 #pragma unroll 2
     for (int b = 0; b < nb; ++b) {
         const uint2 w = __ldg(qw + b * 32);
@@ -166,11 +167,11 @@ __device__ __forceinline__ float dot_q8_0(const uint8_t *__restrict__ tile, int 
         s = fmaf(b2f(u1, 1) - kOff, x1.y, s);
         s = fmaf(b2f(u1, 2) - kOff, x1.z, s);
         s = fmaf(b2f(u1, 3) - kOff, x1.w, s);
-        acc = fmaf(d, s, acc);
+        acc = fma((double)d, (double)s, acc);
     }
     acc += __shfl_xor_sync(kFull, acc, 1);
     acc += __shfl_xor_sync(kFull, acc, 2);
-    return acc;
+    return (float)acc;
 }
 
 __device__ __forceinline__ float tile_dot(const QMat &m, int tile, const float *xs, int lane) {
@@ -210,54 +211,6 @@ __device__ __forceinline__ void rmsnorm_to_smem(const float *xs_in, const float 
     const float s = (float)(1.0 / sqrt((double)t));
     for (int i = threadIdx.x; i < n; i += kThreads) hs[i] = __fmul_rn(__fmul_rn(xs_in[i], s), __ldg(w + i));
     __syncthreads();
-}
-
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// A grid-wide barrier over co-resident CTAs (the persistent kernel runs as
-// a cooperative launch).  The wait is bounded: after 2 s it records
-// DEV_BARRIER_TIMEOUT and returns false, as does every later barrier, so the
-// kernel ends instead of hanging.
-__device__ __noinline__ bool grid_sync(GridBarrier *bar, int *err) {
-    __shared__ int ok;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        ok = 1;
-        const unsigned g = ld_acquire(&bar->gen);
-        __threadfence();
-        const unsigned arrived = atomicAdd(&bar->count, 1u);
-        if (arrived == gridDim.x - 1) {
-            bar->count = 0;
-            __threadfence();
-            st_release(&bar->gen, g + 1);
-        } else {
-            const uint64_t t0 = globaltimer();
-            while (ld_acquire(&bar->gen) == g) {
-                if (globaltimer() - t0 > 2000000000ull) {
-                    atomicExch(err, DEV_BARRIER_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        if (ok && *(volatile int *)err != 0) ok = 0;
-    }
-    __syncthreads();
-    return ok != 0;
 }
 
 // ------------------------------------------------------------- phases --
@@ -332,61 +285,61 @@ __device__ void phase_attn(const DevModel &dm, int l, int t, int n, int item, ui
     const Layer &L = dm.layer[l];
     float *qh = sm.vec;              // HD
     float *e = sm.vec + HD;          // kAttnChunk
-    float *part = sm.vec + HD + kAttnChunk;  // kThreads * 4 (partial V sums)
+    float *part = sm.vec + HD + kAttnChunk;  // kThreads * 4 doubles (partial V sums)
     __shared__ int last;
     for (int i = threadIdx.x; i < HD; i += kThreads) qh[i] = __ldcg(dm.q + (size_t)t * dm.embd + h * HD + i);
     __syncthreads();
     const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
-    // scores: 4 threads per position, HD/4 dims each
+    // scores: 4 threads per position, HD/4 dims each, accumulated in double
     const int p = threadIdx.x >> 2, sub = threadIdx.x & 3;
     float s = -FLT_MAX;
     {
-        float part_s = 0.f;
+        double part_s = 0.0;
         if (p < cnt) {
             const float *kr = L.kv + (size_t)(p0 + p) * dm.kvd + kvh * HD;
             for (int d = sub * 4; d < HD; d += 16) {
                 const float4 k4 = __ldcg(reinterpret_cast<const float4 *>(kr + d));
-                part_s = fmaf(qh[d], k4.x, part_s);
-                part_s = fmaf(qh[d + 1], k4.y, part_s);
-                part_s = fmaf(qh[d + 2], k4.z, part_s);
-                part_s = fmaf(qh[d + 3], k4.w, part_s);
+                part_s = fma((double)qh[d], (double)k4.x, part_s);
+                part_s = fma((double)qh[d + 1], (double)k4.y, part_s);
+                part_s = fma((double)qh[d + 2], (double)k4.z, part_s);
+                part_s = fma((double)qh[d + 3], (double)k4.w, part_s);
             }
         }
         part_s += __shfl_xor_sync(kFull, part_s, 1);
         part_s += __shfl_xor_sync(kFull, part_s, 2);
-        if (p < cnt) s = __fmul_rn(part_s, dm.scale);
+        if (p < cnt) s = __fmul_rn((float)part_s, dm.scale);
     }
     const float mx = block_max(s, sm.red);
-    float ev = 0.f;
-    if (p < cnt && sub == 0) {
-        ev = (float)exp((double)__fsub_rn(s, mx));
-        e[p] = ev;
-    }
-    const float lsum = block_sum(ev, sm.red);  // includes the __syncthreads that publishes e[]
-    // V sum: thread (d4, g): float4 d4 of the head, positions g, g+G, ...
+    if (p < cnt && sub == 0) e[p] = (float)exp((double)__fsub_rn(s, mx));
+    __syncthreads();
+    // V sum: thread (d4, g): float4 d4 of the head, positions g, g+G, ..., in double
     const int nd4 = HD / 4, G = kThreads / nd4;
     const int d4 = threadIdx.x % nd4, g = threadIdx.x / nd4;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    double o0 = 0, o1 = 0, o2 = 0, o3 = 0;
     for (int pp = g; pp < cnt; pp += G) {
-        const float w = e[pp];
+        const double w = e[pp];
         const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(L.kv + ((size_t)dm.ctx + p0 + pp) * dm.kvd + kvh * HD) + d4);
-        o.x = fmaf(w, v4.x, o.x);
-        o.y = fmaf(w, v4.y, o.y);
-        o.z = fmaf(w, v4.z, o.z);
-        o.w = fmaf(w, v4.w, o.w);
+        o0 = fma(w, (double)v4.x, o0);
+        o1 = fma(w, (double)v4.y, o1);
+        o2 = fma(w, (double)v4.z, o2);
+        o3 = fma(w, (double)v4.w, o3);
     }
-    reinterpret_cast<float4 *>(part)[threadIdx.x] = o;
+    double *dpart = reinterpret_cast<double *>(part);
+    dpart[threadIdx.x * 4 + 0] = o0, dpart[threadIdx.x * 4 + 1] = o1;
+    dpart[threadIdx.x * 4 + 2] = o2, dpart[threadIdx.x * 4 + 3] = o3;
     __syncthreads();
     const size_t th = (size_t)t * dm.heads + h;
     if (threadIdx.x < nd4) {
-        float4 tot = reinterpret_cast<float4 *>(part)[threadIdx.x];
-        for (int k = 1; k < G; ++k) {
-            const float4 v = reinterpret_cast<float4 *>(part)[threadIdx.x + k * nd4];
-            tot.x += v.x, tot.y += v.y, tot.z += v.z, tot.w += v.w;
-        }
-        reinterpret_cast<float4 *>(dm.part_pv + (th * dm.nchunk + c) * HD)[threadIdx.x] = tot;
+        double tot[4] = {0, 0, 0, 0};
+        for (int k = 0; k < G; ++k)
+            for (int j = 0; j < 4; ++j) tot[j] += dpart[(threadIdx.x + k * nd4) * 4 + j];
+        for (int j = 0; j < 4; ++j) dm.part_pv[(th * dm.nchunk + c) * HD + threadIdx.x * 4 + j] = (float)tot[j];
     }
-    if (threadIdx.x == 0) dm.part_ml[th * dm.nchunk + c] = make_float2(mx, lsum);
+    if (threadIdx.x == 0) {
+        double lsum = 0.0;
+        for (int pp = 0; pp < cnt; ++pp) lsum += e[pp];
+        dm.part_ml[th * dm.nchunk + c] = make_float2(mx, (float)lsum);
+    }
     // the last arriving CTA of this head merges its chunks
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -401,15 +354,14 @@ __device__ void phase_attn(const DevModel &dm, int l, int t, int n, int item, ui
     for (int d = threadIdx.x; d < HD; d += kThreads) {
         float M = -FLT_MAX;
         for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(&dm.part_ml[th * dm.nchunk + cc].x));
-        float lt = 0.f, ot = 0.f;
+        double lt = 0.0, ot = 0.0;
         for (int cc = 0; cc < nch; ++cc) {
             const float2 ml = __ldcg(&dm.part_ml[th * dm.nchunk + cc]);
-            const float f = (float)exp((double)__fsub_rn(ml.x, M));
-            lt = fmaf(f, ml.y, lt);
-            ot = fmaf(f, __ldcg(dm.part_pv + (th * dm.nchunk + cc) * HD + d), ot);
+            const double f = exp((double)ml.x - (double)M);
+            lt = fma(f, (double)ml.y, lt);
+            ot = fma(f, (double)__ldcg(dm.part_pv + (th * dm.nchunk + cc) * HD + d), ot);
         }
-        const float a = __fdiv_rn(ot, lt);
-        dm.att[(size_t)t * dm.embd + h * HD + d] = a;
+        dm.att[(size_t)t * dm.embd + h * HD + d] = (float)(ot / lt);
     }
 }
 
@@ -611,51 +563,6 @@ __global__ void k_advance(const DevModel *__restrict__ dmp, int n) {
     dmp->state[1] += n;
 }
 
-// ------------------------------------------------ the persistent kernel --
-
-__global__ void __launch_bounds__(kThreads, 1)
-    k_decode(const DevModel *__restrict__ dmp, GridBarrier *bar, int ntok) {
-    extern __shared__ float smem[];
-    const DevModel &dm = *dmp;
-    Smem sm = smem_views(smem, dm);
-    const int cta = blockIdx.x, ncta = gridDim.x;
-    int pos = (int)__ldcg(dm.state), step = (int)__ldcg(dm.state + 1);
-    int tok = __ldcg(dm.tokens + step);
-    for (int i = 0; i < ntok; ++i) {
-        if (pos >= dm.ctx) {
-            if (cta == 0 && threadIdx.x == 0) atomicExch(dm.err, DEV_CONTEXT_FULL);
-            return;
-        }
-        const int n = pos + 1, nch = (n + kAttnChunk - 1) / kAttnChunk;
-        for (int l = 0; l < dm.layers; ++l) {
-            phase_qkv(dm, l, 0, pos, tok, l == 0, cta, ncta, sm);
-            if (!grid_sync(bar, dm.err)) return;
-            for (int item = cta; item < dm.heads * nch; item += ncta) {
-                phase_attn(dm, l, 0, n, item, dm.att_cnt, sm);
-                __syncthreads();
-            }
-            if (!grid_sync(bar, dm.err)) return;
-            phase_oproj(dm, l, 0, cta, ncta, sm);
-            if (!grid_sync(bar, dm.err)) return;
-            phase_gateup(dm, l, 0, cta, ncta, sm);
-            if (!grid_sync(bar, dm.err)) return;
-            phase_down(dm, l, 0, cta, ncta, sm);
-            if (!grid_sync(bar, dm.err)) return;
-        }
-        phase_head(dm, 0, cta, ncta, sm);
-        if (!grid_sync(bar, dm.err)) return;
-        tok = reduce_argmax(dm, ncta, sm.red);
-        ++pos, ++step;
-        if (cta == 0 && threadIdx.x == 0) dm.tokens[step] = tok;
-        // every CTA reads the partials before any CTA of the next token
-        // overwrites them (its head phase comes after 5 * layers barriers)
-    }
-    if (cta == 0 && threadIdx.x == 0) {
-        dm.state[0] = pos;
-        dm.state[1] = step;
-    }
-}
-
 // ------------------------------------------------------------ loading --
 
 __device__ __forceinline__ int neox_map(int nr, int hd) {  // fused.go:331-334
@@ -690,7 +597,7 @@ __global__ void k_repack(const uint8_t *__restrict__ raw, int rows, int nb, int 
 
 int smem_vec_floats(const Shapes &s) {
     const int vec = s.embd + (s.embd > s.ff ? s.embd : s.ff);
-    const int attn = s.head_dim + kAttnChunk + 4 * kThreads;
+    const int attn = s.head_dim + kAttnChunk + 8 * kThreads;
     return vec > attn ? vec : attn;
 }
 
@@ -722,28 +629,5 @@ void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaSt
 }
 
 void launch_advance(const DevModel *dm, int n, cudaStream_t st) { k_advance<<<1, 1, 0, st>>>(dm, n); }
-
-int persistent_ctas_per_sm(const Shapes &s) {
-    int n = 0;
-    const size_t sh = smem_bytes(s);
-    cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode, kThreads, sh);
-    return n;
-}
-
-cudaError_t launch_decode_persistent(const DevModel *dm, const Shapes &s, GridBarrier *bar, int ntok, int ctas,
-                                     cudaStream_t st) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ctas);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem_bytes(s);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_decode, dm, bar, ntok);
-}
 
 }  // namespace llmb

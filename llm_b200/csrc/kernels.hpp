@@ -12,6 +12,8 @@ enum DeviceError : int {
     DEV_OK = 0,
     DEV_BARRIER_TIMEOUT = 1,  // a grid barrier waited longer than its limit
     DEV_CONTEXT_FULL = 2,     // a token past the context
+    DEV_TAG_TIMEOUT = 3,      // a tagged activation did not arrive in time
+    DEV_RING_TIMEOUT = 4,     // a weight slot did not fill or drain in time
 };
 
 struct GridBarrier {
@@ -56,12 +58,14 @@ void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaSt
 // state += n.
 void launch_advance(const DevModel *dm, int n, cudaStream_t st);
 
-// The persistent decode kernel: ntok tokens, every phase of every layer and
-// the head, one cooperative launch over all SMs with bounded grid barriers.
-cudaError_t launch_decode_persistent(const DevModel *dm, const Shapes &s, GridBarrier *bar, int ntok, int ctas,
-                                     cudaStream_t st);
-
-// CTAs per SM the persistent kernel can keep resident (for the cooperative grid).
-int persistent_ctas_per_sm(const Shapes &s);
+// The warp-specialised persistent decode kernel (decode.cu).
+struct DecConfig {
+    int nslots, slot_bytes, threads;
+    size_t smem;
+};
+DecConfig decode_config(const Shapes &s, int max_tile_bytes, int gate_rows, int qkv_rows);
+cudaError_t launch_decode2(const DecParams &dm, const DecConfig &c, GridBarrier *bar, int ntok, int ctas,
+                           cudaStream_t st);
+int decode2_ctas_per_sm(const DecConfig &c);
 
 }  // namespace llmb

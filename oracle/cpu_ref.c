@@ -605,10 +605,62 @@ typedef struct {
     int r0, r1;
 } mv_job;
 
-static void *mv_worker(void *p) {
-    mv_job *j = p;
-    for (int o = j->r0; o < j->r1; o++) j->dst[o] = matvec_row(j->type, j->in, j->data + (size_t)o * j->row_bytes, j->x);
+static void mv_run(const mv_job *j) {
+    for (int o = j->r0; o < j->r1; o++) j->dst[o] = matvec_row(j->type, j->in, j->data + (size_t)j->row_bytes * o, j->x);
+}
+
+/* A persistent pool of worker threads: each product hands every worker one
+ * contiguous range of rows and waits for all of them. */
+static struct {
+    pthread_mutex_t mu;
+    pthread_cond_t go, done;
+    int nworkers;      /* threads started (the caller is worker 0) */
+    unsigned long gen; /* job generation */
+    int pending;
+    mv_job jobs[64];
+} pool = {PTHREAD_MUTEX_INITIALIZER, PTHREAD_COND_INITIALIZER, PTHREAD_COND_INITIALIZER, 0, 0, 0, {{0}}};
+
+typedef struct {
+    int id;
+} worker_arg;
+
+static void *pool_worker(void *p) {
+    int id = ((worker_arg *)p)->id;
+    free(p);
+    unsigned long seen = 0;
+    for (;;) {
+        pthread_mutex_lock(&pool.mu);
+        while (pool.gen == seen) pthread_cond_wait(&pool.go, &pool.mu);
+        seen = pool.gen;
+        mv_job j = pool.jobs[id];
+        pthread_mutex_unlock(&pool.mu);
+        mv_run(&j);
+        pthread_mutex_lock(&pool.mu);
+        if (--pool.pending == 0) pthread_cond_signal(&pool.done);
+        pthread_mutex_unlock(&pool.mu);
+    }
     return NULL;
+}
+
+static void pool_matvec(int nt, const mv_job *all) {
+    pthread_mutex_lock(&pool.mu);
+    while (pool.nworkers < nt - 1) {
+        worker_arg *a = malloc(sizeof *a);
+        a->id = ++pool.nworkers;
+        pthread_t th;
+        pthread_create(&th, NULL, pool_worker, a);
+        pthread_detach(th);
+    }
+    for (int i = 1; i < nt; i++) pool.jobs[i] = all[i];
+    for (int i = nt; i <= pool.nworkers; i++) pool.jobs[i] = (mv_job){0};
+    pool.pending = pool.nworkers;
+    pool.gen++;
+    pthread_cond_broadcast(&pool.go);
+    pthread_mutex_unlock(&pool.mu);
+    mv_run(&all[0]);
+    pthread_mutex_lock(&pool.mu);
+    while (pool.pending > 0) pthread_cond_wait(&pool.done, &pool.mu);
+    pthread_mutex_unlock(&pool.mu);
 }
 
 /* matvec, cpu.go:142-222: dst = W x for a [in, out] tensor whose rows (ne[0]
@@ -630,19 +682,15 @@ EXPORT int orc_matvec(uint32_t type, int in, int out, const uint8_t *data, const
     size_t row_bytes = (size_t)(in / 32) * bb;
     int nt = g_threads;
     if (nt > 64) nt = 64;
-    /* threads pay off only on large products (the output head) */
-    if (nt <= 1 || (int64_t)out * in < (1 << 22)) {
+    if (nt > out) nt = out;
+    if (nt <= 1 || (int64_t)out * in < (1 << 16)) {
         for (int o = 0; o < out; o++) dst[o] = matvec_row(type, in, data + (size_t)o * row_bytes, x);
         return ORC_OK;
     }
     mv_job jobs[64];
-    pthread_t th[64];
-    for (int i = 0; i < nt; i++) {
+    for (int i = 0; i < nt; i++)
         jobs[i] = (mv_job){type, in, out, row_bytes, data, x, dst, (int)((int64_t)out * i / nt), (int)((int64_t)out * (i + 1) / nt)};
-        if (i > 0) pthread_create(&th[i], NULL, mv_worker, &jobs[i]);
-    }
-    mv_worker(&jobs[0]);
-    for (int i = 1; i < nt; i++) pthread_join(th[i], NULL);
+    pool_matvec(nt, jobs);
     return ORC_OK;
 }
 
