@@ -164,6 +164,30 @@ LLMB_API int llmb_set_layers(llmb_model *m, int layers);
 LLMB_API int llmb_set_knob(const char *name, int64_t value);
 LLMB_API int64_t llmb_get_knob(const char *name);
 
+/* Decode attention that allocates no device memory.  It has no counterpart
+ * in the reference; it exists for callers that cannot call cudaMalloc: a
+ * host whose device memory is a fixed grant made by someone else (the
+ * reference runs as a WebAssembly guest whose GPU memory its host grants up
+ * front), or code that runs where allocation is not allowed.  Such a caller
+ * passes device pointers it already owns:
+ *   q        [heads * head_dim]               the query of one position
+ *   k_cache  [n_pos rows of kv_stride floats] K, head g at g * head_dim
+ *   v_cache  [n_pos rows of kv_stride floats] V, same layout
+ *   out      [heads * head_dim]               softmax(q k / sqrt(head_dim)) v
+ * (the attention of cpu.go:304-335; query head h reads kv head
+ * h / (heads / kv_heads)).  The scratch, split-KV partials, is one
+ * fixed array in device memory (about 1 MiB, held by every GPU that loads
+ * this library until the process exits), so the sizes are limited: at most
+ * 32 heads, head_dim 128 and 4096 positions; larger ones return LLMB_ERR_ARG
+ * before any work.  The first call on a device looks up the array's address
+ * on that device (make it before any stream capture).  Every call shares the
+ * array: calls that overlap on the GPU race, so serialise them (one stream).
+ * No part of the array needs clearing between calls: a call reads only what
+ * it wrote.  Asynchronous on `stream` (a cudaStream_t, NULL for the default
+ * stream); the caller synchronises. */
+LLMB_API int llmb_attention_noalloc(const float *q, const float *k_cache, const float *v_cache, int n_pos, int heads,
+                                    int kv_heads, int head_dim, int kv_stride, float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,7 +31,7 @@ OK, ERR_ARG, ERR_IO, ERR_FORMAT, ERR_BOUND, ERR_CONFIG, ERR_TENSOR, ERR_MEMORY, 
 # Every function include/llm_b200.h declares.
 EXPORTS = ("llmb_open", "llmb_open_reader", "llmb_close", "llmb_last_error", "llmb_get_config", "llmb_memory_used",
            "llmb_get_stats", "llmb_generate", "llmb_prefill_logits", "llmb_generate_logits", "llmb_peek",
-           "llmb_set_layers", "llmb_set_knob", "llmb_get_knob")
+           "llmb_set_layers", "llmb_set_knob", "llmb_get_knob", "llmb_attention_noalloc")
 
 
 class LlmError(RuntimeError):
@@ -86,6 +86,8 @@ def lib() -> C.CDLL:
         L.llmb_set_layers.argtypes, L.llmb_set_layers.restype = [P, I], I
         L.llmb_set_knob.argtypes, L.llmb_set_knob.restype = [C.c_char_p, C.c_int64], I
         L.llmb_get_knob.argtypes, L.llmb_get_knob.restype = [C.c_char_p], C.c_int64
+        L.llmb_attention_noalloc.argtypes = [P, P, P, I, I, I, I, I, P, P]
+        L.llmb_attention_noalloc.restype = I
         _lib = L
     return _lib
 
