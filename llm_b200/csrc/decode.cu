@@ -9,9 +9,8 @@
 //     not depend on activations, so the stream runs ahead across phases,
 //     layers and tokens as far as the ring allows;
 //   - 8 consumer warps compute.  Every tile's blocks are split across the
-//     warps; each warp accumulates its partial row sums in double across
-//     blocks (a block's 8-term sums in paired f32), and the partials meet in
-//     shared memory in a fixed order, so results are deterministic.
+//     warps (paired f32 math); the partials meet in shared memory and
+//     shuffles in a fixed order, so results are deterministic.
 //
 // Activations move between CTAs as 64-bit words {f32 value, u32 tag}
 // written and polled with relaxed GPU-scope accesses (a value and its tag
@@ -40,6 +39,10 @@ constexpr int kCons = 8;                 // consumer warps
 constexpr int kConsThreads = kCons * 32; // 256
 constexpr int kDecThreads = kConsThreads + 32;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+#ifndef LLMB_POLL_SLEEP_NS
+#define LLMB_POLL_SLEEP_NS 64
+#endif
+constexpr unsigned kPollSleepNs = LLMB_POLL_SLEEP_NS;
 
 // ------------------------------------------------------------ primitives --
 
@@ -159,6 +162,7 @@ __device__ __noinline__ bool poll_segs(const Seg (&sg)[NS], int *err) {
             if (!p) continue;
             const uint32_t tag = sg[j].tag;
             while ((uint32_t)(v[2 * k] >> 32) != tag || (uint32_t)(v[2 * k + 1] >> 32) != tag) {
+                __nanosleep(kPollSleepNs);  // back off: every waiting thread polls the same few lines
                 ld_relaxed2(p, v[2 * k], v[2 * k + 1]);
                 if ((++spins & 255) == 0) {
                     if (read_err(err)) return false;
@@ -235,8 +239,8 @@ __device__ __forceinline__ float b2f(uint32_t v, int k) {
 }
 
 // Phase timeline (DevModel::trace): for event ev of this CTA, stamps 0..2
-// (entry, input ready, exit) and the time the phase spent waiting for weight
-// slots (field 3, accumulated by unit_rows).
+// (entry, input ready, exit, globaltimer ns) and the SM cycles the phase
+// spent waiting for weight slots (field 3, accumulated by unit_rows).
 __shared__ uint64_t s_ring_wait;
 
 struct Trace {
@@ -291,19 +295,21 @@ struct DecSmem {
 
 // --------------------------------------------------------- dot products --
 // A tile of 8 rows in shared memory; lane (r, q) = (lane / 4, lane % 4).
-// Returns the lane's partial over blocks [b0, b1), in double.
+// Returns the lane's partial over blocks [b0, b1).  Everything here is on
+// the latency-critical path of a phase, so it stays in f32: double
+// conversions and FMAs cost hundreds of cycles of latency per block here.
 
 // Q4_0 / Q4_1 with the activation in paired layout: for block b, pair j
 // (0..15) = (x[32b + j], x[32b + 16 + j]), so lane q reads pairs 4q..4q+3.
 template <bool Q41>
-__device__ __forceinline__ double dot_q4(const uint8_t *tile, int nb, const float2 *xp, int b0, int b1, int lane) {
+__device__ __forceinline__ float dot_q4(const uint8_t *tile, int nb, const float2 *xp, int b0, int b1, int lane) {
     const int r = lane >> 2, q = lane & 3;
     const uint32_t *qw = reinterpret_cast<const uint32_t *>(tile) + r * 4 + q;
     const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 128) + r;
     const __half *mp = dp + nb * 8;
     const float off = Q41 ? 8388608.f : 8388616.f;
     const float2 off2 = make_float2(off, off);
-    double acc = 0.0;
+    float acc = 0.f;
 #pragma unroll 4
     for (int b = b0; b < b1; ++b) {
         const uint32_t w = qw[b * 32];
@@ -324,21 +330,21 @@ __device__ __forceinline__ double dot_q4(const uint8_t *tile, int nb, const floa
             const float mn = __half2float(mp[b * 8]);
             const float2 sx2 = __fadd2_rn(__fadd2_rn(make_float2(xa.x, xa.y), make_float2(xa.z, xa.w)),
                                           __fadd2_rn(make_float2(xb.x, xb.y), make_float2(xb.z, xb.w)));
-            acc = fma((double)d, (double)sum, fma((double)mn, (double)(sx2.x + sx2.y), acc));
+            acc = fmaf(d, sum, fmaf(mn, sx2.x + sx2.y, acc));
         } else {
-            acc = fma((double)d, (double)sum, acc);
+            acc = fmaf(d, sum, acc);
         }
     }
     return acc;
 }
 
 // Q8_0 with the activation in plain layout: lane q owns elements 8q..8q+7.
-__device__ __forceinline__ double dot_q8(const uint8_t *tile, int nb, const float *x, int b0, int b1, int lane) {
+__device__ __forceinline__ float dot_q8(const uint8_t *tile, int nb, const float *x, int b0, int b1, int lane) {
     const int r = lane >> 2, q = lane & 3;
     const uint2 *qw = reinterpret_cast<const uint2 *>(tile) + r * 4 + q;
     const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 256) + r;
     constexpr float off = 8388736.f;
-    double acc = 0.0;
+    float acc = 0.f;
 #pragma unroll 4
     for (int b = b0; b < b1; ++b) {
         const uint2 w = qw[b * 32];
@@ -351,12 +357,12 @@ __device__ __forceinline__ double dot_q8(const uint8_t *tile, int nb, const floa
         s = __ffma2_rn(__fadd2_rn(make_float2(b2f(u0, 2), b2f(u0, 3)), o2), make_float2(xa.z, xa.w), s);
         s = __ffma2_rn(__fadd2_rn(make_float2(b2f(u1, 0), b2f(u1, 1)), o2), make_float2(xb.x, xb.y), s);
         s = __ffma2_rn(__fadd2_rn(make_float2(b2f(u1, 2), b2f(u1, 3)), o2), make_float2(xb.z, xb.w), s);
-        acc = fma((double)d, (double)(s.x + s.y), acc);
+        acc = fmaf(d, s.x + s.y, acc);
     }
     return acc;
 }
 
-__device__ __forceinline__ double dot_tile(int type, const uint8_t *tile, int nb, const DecSmem &sm, int b0, int b1,
+__device__ __forceinline__ float dot_tile(int type, const uint8_t *tile, int nb, const DecSmem &sm, int b0, int b1,
                                            int lane) {
     if (type == 8) return dot_q8(tile, nb, sm.xq8, b0, b1, lane);
     if (type == 3) return dot_q4<true>(tile, nb, reinterpret_cast<const float2 *>(sm.xv), b0, b1, lane);
@@ -375,19 +381,6 @@ __device__ __forceinline__ void stage_vector(const float *src, int n, const DecS
         sm.xv[b * 32 + 2 * pj + (j >> 4)] = v;
         if (q8) sm.xq8[i] = v;
     }
-}
-
-__device__ __forceinline__ float cons_sum(float v, float *red) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    cons_sync();
-    if (l == 0) red[w] = v;
-    cons_sync();
-    float t = l < kCons ? red[l] : 0.f;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
-    return t;
 }
 
 __device__ __forceinline__ float cons_max(float v, float *red) {
@@ -416,24 +409,41 @@ struct NormW {
     }
 };
 
-// RMSNorm (cpu.go:81-98) of sm.xs (E floats) with weights nw into the staging layouts.
-__device__ __forceinline__ void norm_stage(const DecParams &dm, const NormW &nw, const DecSmem &sm, bool q8) {
+// RMSNorm (cpu.go:81-98), folded: stages x * w (into the layouts the dot
+// products read) and leaves the warps' partial sums of squares in red[32..39];
+// the scalar 1 / rms (norm_scale) multiplies the dot products' results
+// instead of every element, which keeps the sum of squares, the division and
+// the square root off the path to the first dot product.  (x * w) * s and
+// cpu.go's (x * s) * w differ only in rounding.
+__device__ __forceinline__ void norm_fold(const DecParams &dm, const NormW &nw, const DecSmem &sm, bool q8) {
     const int E = dm.embd;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < E; i += kConsThreads) ss = fmaf(sm.xs[i], sm.xs[i], ss);
-    ss = cons_sum(ss, sm.red);
-    const float t = __fadd_rn(__fdiv_rn(ss, (float)E), dm.eps);
-    const float s = (float)(1.0 / sqrt((double)t));
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int i = threadIdx.x + k * kConsThreads;
         if (i >= E) break;
-        const float v = __fmul_rn(__fmul_rn(sm.xs[i], s), nw.w[k]);
+        const float x = sm.xs[i];
+        ss = fmaf(x, x, ss);
+        const float v = __fmul_rn(x, nw.w[k]);
         const int b = i >> 5, j = i & 31, pj = j & 15;
         sm.xv[b * 32 + 2 * pj + (j >> 4)] = v;
         if (q8) sm.xq8[i] = v;
     }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+    if ((threadIdx.x & 31) == 0) sm.red[32 + (threadIdx.x >> 5)] = ss;
     cons_sync();
+}
+
+// 1 / sqrt(mean of squares + eps), from norm_fold's partials (fixed order):
+// cpu.go:94 rounds 1/sqrt computed in double to float; rsqrt in double is
+// within an ulp of that double, far below float's rounding.
+__device__ __forceinline__ float norm_scale(const DecParams &dm, const DecSmem &sm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCons; ++w) ss += sm.red[32 + w];
+    const float t = __fadd_rn(__fdiv_rn(ss, (float)dm.embd), dm.eps);
+    return (float)rsqrt((double)t);
 }
 
 // ------------------------------------------------------------- consume --
@@ -444,64 +454,88 @@ struct Ring {
     unsigned u;  // units consumed so far
 };
 
-__device__ __forceinline__ bool ring_wait(const DecSmem &sm, const Ring &rg, int *err) {
-    const int slot = rg.u % rg.nslots;
-    const unsigned parity = (rg.u / rg.nslots) & 1;
-    if (mbar_try_wait(sm.full + slot, parity)) return true;
-    const uint64_t t0 = gtimer();
-    while (!mbar_try_wait(sm.full + slot, parity)) {
-        if (read_err(err)) return false;
-        if (gtimer() - t0 > kWaitNs) {
-            atomicExch(err, DEV_RING_TIMEOUT);
-            return false;
+// The shared-memory views the tile pipeline needs (by value, so the
+// out-of-line unit_rows below takes no reference to kernel parameters).
+struct UnitCtx {
+    uint64_t *full, *empty;
+    uint8_t *ring;
+    float *xv, *xq8, *part, *rows;
+};
+
+// Computes the rows of one unit (k tiles of matrix m) into c.rows[k * 8]
+// (row i of the unit).  All consumer warps take part: with k >= 8 each warp
+// takes whole tiles, otherwise every tile's blocks are split across the
+// warps, whose partials meet through shared memory and three shuffles, in a
+// fixed order.
+__device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const UnitCtx &c, const int nslots,
+                                             const int slot_bytes, const unsigned u, int *err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t w0 = threadIdx.x == 0 ? clock64() : 0;
+    const int sl = u % nslots;
+    bool ok = true;
+    if (!mbar_try_wait(c.full + sl, (u / nslots) & 1)) {
+        const uint64_t t0 = gtimer();
+        while (!mbar_try_wait(c.full + sl, (u / nslots) & 1)) {
+            if (read_err(err)) {
+                ok = false;
+                break;
+            }
+            if (gtimer() - t0 > kWaitNs) {
+                atomicExch(err, DEV_RING_TIMEOUT);
+                ok = false;
+                break;
+            }
         }
     }
-    return true;
-}
-
-__device__ __forceinline__ void ring_release(const DecSmem &sm, Ring &rg) {
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(sm.empty + rg.u % rg.nslots);
-    rg.u++;
-}
-
-// Computes the rows of one unit (k tiles of matrix m, the first is tile t0)
-// into sm.rows[k * 8] (row i of the unit).  All consumer warps take part.
-__device__ __forceinline__ bool unit_rows(const QMat &m, int k, const DecSmem &sm, Ring &rg, int *err) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t w0 = threadIdx.x == 0 ? gtimer() : 0;
-    if (cons_or(!ring_wait(sm, rg, err))) return false;
-    if (threadIdx.x == 0) s_ring_wait += gtimer() - w0;
-    const uint8_t *slot = sm.ring + (size_t)(rg.u % rg.nslots) * rg.slot_bytes;
+    if (cons_or(!ok)) return false;
+    if (threadIdx.x == 0) s_ring_wait += clock64() - w0;
+    const uint8_t *slot = c.ring + (size_t)sl * slot_bytes;
+    DecSmem sm;
+    sm.xv = c.xv, sm.xq8 = c.xq8;
     if (k >= kCons) {
         for (int i = warp; i < k; i += kCons) {
-            double a = dot_tile(m.type, slot + (size_t)i * m.tile_bytes, m.nb, sm, 0, m.nb, lane);
+            float a = dot_tile(m.type, slot + (size_t)i * m.tile_bytes, m.nb, sm, 0, m.nb, lane);
             a += __shfl_xor_sync(kFull, a, 1);
             a += __shfl_xor_sync(kFull, a, 2);
-            if ((lane & 3) == 0) sm.rows[i * 8 + (lane >> 2)] = (float)a;
+            if ((lane & 3) == 0) c.rows[i * 8 + (lane >> 2)] = a;
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(c.empty + sl);
     } else {
         const int parts = kCons / k;
         const int tile = warp / parts, part = warp % parts;
-        double a = 0.0;
+        float a = 0.f;
         if (tile < k) {
             const int b0 = m.nb * part / parts, b1 = m.nb * (part + 1) / parts;
             a = dot_tile(m.type, slot + (size_t)tile * m.tile_bytes, m.nb, sm, b0, b1, lane);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(c.empty + sl);  // the slot is free once this warp's reads are done
         a += __shfl_xor_sync(kFull, a, 1);
         a += __shfl_xor_sync(kFull, a, 2);
-        if ((lane & 3) == 0) sm.part[warp * 8 + (lane >> 2)] = a;
+        // partial of (row r, warp w) -> part[r * 8 + w]: the 8 parts of a row are 8 consecutive lanes
+        if ((lane & 3) == 0) c.part[(lane >> 2) * 8 + warp] = a;
         cons_sync();
-        if (threadIdx.x < k * 8) {
-            const int t = threadIdx.x >> 3, r = threadIdx.x & 7;
-            double s = 0.0;
-            for (int p = 0; p < parts; ++p) s += sm.part[(t * parts + p) * 8 + r];
-            sm.rows[threadIdx.x] = (float)s;
+        if (threadIdx.x < 64) {
+            // thread (r, w) = (t / 8, t % 8); warps w = tile * parts + p
+            float v = c.part[threadIdx.x];
+            const int w = threadIdx.x & 7;
+            // sum over p within each tile's group of `parts` consecutive warps
+            if (parts >= 2) v += __shfl_xor_sync(kFull, v, 1);
+            if (parts >= 4) v += __shfl_xor_sync(kFull, v, 2);
+            if (parts >= 8) v += __shfl_xor_sync(kFull, v, 4);
+            if (w % parts == 0 && w / parts < k) c.rows[(w / parts) * 8 + (threadIdx.x >> 3)] = v;
         }
     }
-    ring_release(sm, rg);
     cons_sync();
     return true;
+}
+
+__device__ __forceinline__ bool unit_rows(const QMat &m, int k, const DecSmem &sm, Ring &rg, int *err) {
+    const UnitCtx c{sm.full, sm.empty, sm.ring, sm.xv, sm.xq8, reinterpret_cast<float *>(sm.part), sm.rows};
+    const bool ok = unit_rows_nl(m, k, c, rg.nslots, rg.slot_bytes, rg.u, err);
+    rg.u++;
+    return ok;
 }
 
 // ---------------------------------------------------------------- tags --
@@ -522,6 +556,7 @@ __device__ __forceinline__ bool prod_unit(const DecSmem &sm, int nslots, int slo
     if (!mbar_try_wait(sm.empty + slot, parity)) {
         const uint64_t t0 = gtimer();
         while (!mbar_try_wait(sm.empty + slot, parity)) {
+            __nanosleep(256);  // the producer runs ahead: leave the scheduler to the consumer warps
             if (read_err(err)) return false;
             if (gtimer() - t0 > kWaitNs) {
                 atomicExch(err, DEV_RING_TIMEOUT);
@@ -531,6 +566,38 @@ __device__ __forceinline__ bool prod_unit(const DecSmem &sm, int nslots, int slo
     }
     mbar_expect_tx(sm.full + slot, bytes);
     bulk_g2s(sm.ring + (size_t)slot * slot_bytes, src, bytes, sm.full + slot);
+    u++;
+    return true;
+}
+
+// Gate and up tiles of a CTA travel as one unit when they have one format and
+// fit one slot (the producer copies both ranges into the slot).
+__device__ __forceinline__ bool gu_fused(const Layer &L, const Share &sg, int slot_bytes) {
+    const int n = sg.b - sg.a;
+    return L.gate.type == L.up.type && L.gate.nb == L.up.nb && 2 * n * L.gate.tile_bytes <= slot_bytes &&
+           2 * n <= kConsThreads / 8;
+}
+
+// One unit made of two ranges (gate tiles, then up tiles), one slot, one barrier.
+__device__ __forceinline__ bool prod_unit2(const DecSmem &sm, int nslots, int slot_bytes, unsigned &u,
+                                           const uint8_t *src1, unsigned bytes1, const uint8_t *src2, unsigned bytes2,
+                                           int *err) {
+    const int slot = u % nslots;
+    const unsigned parity = ((u / nslots) & 1) ^ 1;
+    if (!mbar_try_wait(sm.empty + slot, parity)) {
+        const uint64_t t0 = gtimer();
+        while (!mbar_try_wait(sm.empty + slot, parity)) {
+            __nanosleep(256);
+            if (read_err(err)) return false;
+            if (gtimer() - t0 > kWaitNs) {
+                atomicExch(err, DEV_RING_TIMEOUT);
+                return false;
+            }
+        }
+    }
+    mbar_expect_tx(sm.full + slot, bytes1 + bytes2);
+    bulk_g2s(sm.ring + (size_t)slot * slot_bytes, src1, bytes1, sm.full + slot);
+    bulk_g2s(sm.ring + (size_t)slot * slot_bytes + bytes1, src2, bytes2, sm.full + slot);
     u++;
     return true;
 }
@@ -568,8 +635,15 @@ __device__ void producer(const DecParams &dm, const DecSmem &sm, int nslots, int
                 }
             }
             if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.o, share(L.o, cta, ncta, slot_bytes), dm.err);
-            if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.gate, share(L.gate, cta, ncta, slot_bytes), dm.err);
-            if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.up, share(L.up, cta, ncta, slot_bytes), dm.err);
+            const Share sg = share(L.gate, cta, ncta, slot_bytes);
+            if (ok && sg.b > sg.a && gu_fused(L, sg, slot_bytes)) {
+                const unsigned half = (unsigned)((sg.b - sg.a) * L.gate.tile_bytes);
+                ok = prod_unit2(sm, nslots, slot_bytes, u, L.gate.tiles + (size_t)sg.a * L.gate.tile_bytes, half,
+                                L.up.tiles + (size_t)sg.a * L.up.tile_bytes, half, dm.err);
+            } else {
+                if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.gate, sg, dm.err);
+                if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.up, share(L.up, cta, ncta, slot_bytes), dm.err);
+            }
             if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.down, share(L.down, cta, ncta, slot_bytes), dm.err);
         }
         if (ok) ok = prod_share(sm, nslots, slot_bytes, u, dm.head, share(dm.head, cta, ncta, slot_bytes), dm.err);
@@ -637,7 +711,8 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
     }
     tk.tr.stamp(ev, 1);
     const bool q8 = L.q.type == 8 || L.k.type == 8 || L.v.type == 8;
-    norm_stage(dm, nw, sm, q8);
+    norm_fold(dm, nw, sm, q8);
+    const float nsc = norm_scale(dm, sm);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
     for (int t = a; t < b; ++t) {
         const int seg = t < nq ? 0 : t < nq + nk ? 1 : 2;
@@ -648,10 +723,10 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
             const int r = threadIdx.x, row = lt * 8 + r;
             const float *pre = sm.pre + 3 * ((t - a) * 8);
             const bool has_bias = (seg == 0 ? L.bq : seg == 1 ? L.bk : L.bv) != nullptr;
-            float v = sm.rows[r];
+            float v = __fmul_rn(sm.rows[r], nsc);
             if (has_bias) v = __fadd_rn(v, pre[3 * r]);
             if (seg < 2) {
-                float o = sm.rows[r ^ 1];
+                float o = __fmul_rn(sm.rows[r ^ 1], nsc);
                 if (has_bias) o = __fadd_rn(o, pre[3 * (r ^ 1)]);
                 const float2 cs = make_float2(pre[3 * r + 1], pre[3 * r + 2]);
                 if ((r & 1) == 0) v = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(o, cs.y));
@@ -687,7 +762,7 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // (cp.async) before the item waits for the token's q, k, v.  With one chunk
 // the item writes the head's output; otherwise its partial, chunk-major
 // (ll_pv[c][h][d], ll_ml[c][h][{max, sum}]), for the output projection to
-// merge.  Dot products and sums are accumulated in double.
+// merge.  f32 arithmetic, the exp in double as cpu.go:321.
 template <int HD>
 __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, int nch, const DecSmem &sm) {
     constexpr int KS = HD + 16;  // shared row stride: conflict-free 4-threads-per-row reads
@@ -699,7 +774,7 @@ __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, i
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
     const uint32_t otag = tag_of(tk.epoch, dm.layers, l, PH_ATT);
     float *qh = sm.att, *kc = sm.att + HD, *vc = sm.att + 2 * HD, *e = sm.att + 3 * HD;
-    double *part = reinterpret_cast<double *>(sm.att + 3 * HD + kAttnChunk);  // kConsThreads x 4 doubles
+    float *part = sm.att + 3 * HD + kAttnChunk;  // kConsThreads x 4 floats
     float *ks = sm.kvs, *vs = sm.kvs + kAttnChunk * KS;
     const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
     const bool has_cur = p0 + cnt == n;
@@ -725,65 +800,100 @@ __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, i
     const int p = threadIdx.x >> 2, sub = threadIdx.x & 3;
     float s = -FLT_MAX;
     {
-        double ps0 = 0.0, ps1 = 0.0;
+        float ps0 = 0.f, ps1 = 0.f;
         if (p < cnt) {
 #pragma unroll
             for (int j = 0; j < HD / 16; ++j) {
                 const int d = 4 * (sub + 4 * j);
                 const float4 k4 = *reinterpret_cast<const float4 *>(ks + p * KS + d);
                 const float4 q4 = *reinterpret_cast<const float4 *>(qh + d);
-                ps0 = fma((double)q4.x, (double)k4.x, ps0);
-                ps1 = fma((double)q4.y, (double)k4.y, ps1);
-                ps0 = fma((double)q4.z, (double)k4.z, ps0);
-                ps1 = fma((double)q4.w, (double)k4.w, ps1);
+                ps0 = fmaf(q4.x, k4.x, ps0);
+                ps1 = fmaf(q4.y, k4.y, ps1);
+                ps0 = fmaf(q4.z, k4.z, ps0);
+                ps1 = fmaf(q4.w, k4.w, ps1);
             }
         }
-        double ps = ps0 + ps1;
+        float ps = ps0 + ps1;
         ps += __shfl_xor_sync(kFull, ps, 1);
         ps += __shfl_xor_sync(kFull, ps, 2);
-        if (p < cnt) s = __fmul_rn((float)ps, dm.scale);
+        if (p < cnt) s = __fmul_rn(ps, dm.scale);
     }
     const float mx = cons_max(s, sm.red);
-    if (p < cnt && sub == 0) e[p] = (float)exp((double)__fsub_rn(s, mx));
+    if (p < cnt && sub == 0) e[p] = (float)exp((double)__fsub_rn(s, mx));  // as cpu.go:321
     cons_sync();
     constexpr int G = kConsThreads / V4;
     const int d4 = threadIdx.x % V4, g = threadIdx.x / V4;
-    double o0 = 0, o1 = 0, o2 = 0, o3 = 0;
+    float o0 = 0, o1 = 0, o2 = 0, o3 = 0;
 #pragma unroll
     for (int k = 0; k < kAttnChunk / G; ++k) {
         const int pp = g + k * G;
         if (pp < cnt) {
-            const double w = e[pp];
+            const float w = e[pp];
             const float4 v4 = *reinterpret_cast<const float4 *>(vs + pp * KS + d4 * 4);
-            o0 = fma(w, (double)v4.x, o0);
-            o1 = fma(w, (double)v4.y, o1);
-            o2 = fma(w, (double)v4.z, o2);
-            o3 = fma(w, (double)v4.w, o3);
+            o0 = fmaf(w, v4.x, o0);
+            o1 = fmaf(w, v4.y, o1);
+            o2 = fmaf(w, v4.z, o2);
+            o3 = fmaf(w, v4.w, o3);
         }
     }
     part[threadIdx.x * 4 + 0] = o0, part[threadIdx.x * 4 + 1] = o1;
     part[threadIdx.x * 4 + 2] = o2, part[threadIdx.x * 4 + 3] = o3;
     cons_sync();
+    float *own = sm.merge;  // the merging item's own partial: V sum [HD], max, sum of exp
     if (threadIdx.x < V4) {
-        double t4[4] = {0, 0, 0, 0};
+        float t4[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int k = 0; k < G; ++k)
 #pragma unroll
             for (int j = 0; j < 4; ++j) t4[j] += part[(threadIdx.x + k * V4) * 4 + j];
-        double lsum = 0.0;
+        float lsum = 0.f;
         for (int pp = 0; pp < cnt; ++pp) lsum += e[pp];
+        const size_t pi = (size_t)h * dm.nchunk + c;  // head-major: a head's chunks are contiguous
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int d = threadIdx.x * 4 + j;
-            if (nch == 1) ll_put(dm.ll_att + h * HD + d, (float)(t4[j] / lsum), otag);
-            else ll_put(dm.ll_pv + ((size_t)c * dm.heads + h) * HD + d, (float)t4[j], otag);
+            if (nch == 1) ll_put(dm.ll_att + h * HD + d, __fdiv_rn(t4[j], lsum), otag);
+            else if (has_cur) own[d] = t4[j];
+            else ll_put(dm.ll_pv + pi * HD + d, t4[j], otag);
         }
         if (nch > 1 && threadIdx.x == 0) {
-            ll_put(dm.ll_ml + ((size_t)c * dm.heads + h) * 2, mx, otag);
-            ll_put(dm.ll_ml + ((size_t)c * dm.heads + h) * 2 + 1, (float)lsum, otag);
+            if (has_cur) {
+                own[HD] = mx, own[HD + 1] = lsum;
+            } else {
+                ll_put(dm.ll_ml + pi * 2, mx, otag);
+                ll_put(dm.ll_ml + pi * 2 + 1, lsum, otag);
+            }
         }
     }
     cons_sync();
+    if (nch > 1 && has_cur) {
+        // The item holding the current position merges the head's other chunks
+        // (kernels_fused.go:150-170) in groups of up to 8, running max and sums
+        // in double, and publishes the head's output.
+        float *gpv = own + HD + 16, *gml = gpv + 8 * HD;
+        const int d = threadIdx.x;
+        double M = own[HD], Ls = own[HD + 1], O = d < HD ? (double)own[d] : 0.0;
+        for (int c0 = 0; c0 < nch - 1; c0 += 8) {
+            const int gn = min(8, nch - 1 - c0);
+            const size_t pi = (size_t)h * dm.nchunk + c0;
+            if (cons_or(!poll_two(dm.ll_pv + pi * HD, gn * HD, otag, gpv, dm.ll_ml + pi * 2, gn * 2, otag, gml, dm.err)))
+                return false;
+            if (d < HD) {
+                double Mn = M;
+                for (int k = 0; k < gn; ++k) Mn = fmax(Mn, (double)gml[2 * k]);
+                const double rs = exp(M - Mn);
+                O *= rs, Ls *= rs;
+                for (int k = 0; k < gn; ++k) {
+                    const double f = exp((double)gml[2 * k] - Mn);
+                    Ls = fma(f, (double)gml[2 * k + 1], Ls);
+                    O = fma(f, (double)gpv[k * HD + d], O);
+                }
+                M = Mn;
+            }
+            cons_sync();
+        }
+        if (d < HD) ll_put(dm.ll_att + h * HD + d, (float)(O / Ls), otag);
+    }
     tk.tr.stamp(ev, 2);
     return true;
 }
@@ -792,76 +902,22 @@ __device__ bool ph_attn(const DecParams &dm, int l, const Tok &tk, int item, int
     return dm.head_dim == 128 ? ph_attn_t<128>(dm, l, tk, item, nch, sm) : ph_attn_t<64>(dm, l, tk, item, nch, sm);
 }
 
-// The merged attention of all heads into sm.xs (E floats), and the
-// residual rows [r0, r0 + nr) into sm.gate: with several chunks, the chunks'
-// partials are merged (kernels_fused.go:150-170) in groups of up to 8, in
-// double.
-__device__ bool gather_att(const DecParams &dm, int l, const Tok &tk, int nch, const DecSmem &sm, int r0, int nr,
-                           uint32_t xtag) {
-    const int HD = dm.head_dim, E = dm.embd, H = dm.heads;
+// The attention of all heads into sm.xs (E floats), and the residual rows
+// [r0, r0 + nr) into sm.gate.
+__device__ bool gather_att(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, int r0, int nr, uint32_t xtag) {
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_ATT);
-    if (nch == 1) return !cons_or(!poll_two(dm.ll_att, E, tag, sm.xs, dm.ll_x + r0, nr, xtag, sm.gate, dm.err));
-    // running merge over groups of up to 8 chunks: per head the max M and the
-    // sum L of the chunks' exp sums, rescaled; per element the weighted sum O
-    double accO[4];
-    const int per = (E + kConsThreads - 1) / kConsThreads;  // <= 4 (embd <= 1024)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) accO[k] = 0;
-    double *hM = reinterpret_cast<double *>(sm.merge + 8 * E + 16 * H);  // [H] running max
-    double *hL = hM + H;                                                  // [H] running sum
-    double *fc = hL + H;                                                  // [8][H] chunk factors, then [H] rescale
-    for (int i = threadIdx.x; i < H; i += kConsThreads) hM[i] = -1e300, hL[i] = 0;
-    for (int c0 = 0; c0 < nch; c0 += 8) {
-        const int gn = min(8, nch - c0);
-        float *pv = sm.merge, *ml = sm.merge + 8 * E;
-        const bool first = c0 == 0;
-        const Seg sg[3] = {{dm.ll_pv + (size_t)c0 * H * HD, gn * E, tag, pv},
-                           {dm.ll_ml + (size_t)c0 * H * 2, gn * H * 2, tag, ml},
-                           {dm.ll_x + r0, first ? nr : 0, xtag, sm.gate}};
-        if (cons_or(!poll_segs(sg, dm.err))) return false;
-        for (int h = threadIdx.x; h < H; h += kConsThreads) {
-            double M = hM[h];
-            for (int c = 0; c < gn; ++c) M = fmax(M, (double)ml[(c * H + h) * 2]);
-            const double rs = exp(hM[h] - M);
-            double Ls = hL[h] * rs;
-            for (int c = 0; c < gn; ++c) {
-                const double f = exp((double)ml[(c * H + h) * 2] - M);
-                fc[c * H + h] = f;
-                Ls = fma(f, (double)ml[(c * H + h) * 2 + 1], Ls);
-            }
-            fc[8 * H + h] = rs;
-            hM[h] = M, hL[h] = Ls;
-        }
-        cons_sync();
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int i = threadIdx.x + k * kConsThreads;
-            if (k >= per || i >= E) continue;
-            const int h = i / HD;
-            double O = accO[k] * fc[8 * H + h];
-            for (int c = 0; c < gn; ++c) O = fma(fc[c * H + h], (double)pv[c * E + i], O);
-            accO[k] = O;
-        }
-        cons_sync();
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int i = threadIdx.x + k * kConsThreads;
-        if (k < per && i < E) sm.xs[i] = (float)(accO[k] / hL[i / HD]);
-    }
-    cons_sync();
-    return true;
+    return !cons_or(!poll_two(dm.ll_att, dm.embd, tag, sm.xs, dm.ll_x + r0, nr, xtag, sm.gate, dm.err));
 }
 
 // K3: x += Wo att (cpu.go:336-339).
-__device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, int nch, const DecSmem &sm, Ring &rg) {
+__device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Layer &L = dm.layer[l];
     const Share s = share(L.o, blockIdx.x, gridDim.x, rg.slot_bytes);
     if (s.b <= s.a) return true;
     const uint32_t tin = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
     const int ev = l * 5 + PH_O;
     tk.tr.stamp(ev, 0);
-    if (!gather_att(dm, l, tk, nch, sm, s.a * 8, (s.b - s.a) * 8, tin)) return false;
+    if (!gather_att(dm, l, tk, sm, s.a * 8, (s.b - s.a) * 8, tin)) return false;
     tk.tr.stamp(ev, 1);
     stage_vector(sm.xs, dm.embd, sm, L.o.type == 8);
     cons_sync();
@@ -892,26 +948,37 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     nw.load(L.ffn_norm, E);
     if (cons_or(!poll_vec(dm.ll_x, E, tin, sm.xs, dm.err))) return false;
     tk.tr.stamp(ev, 1);
-    norm_stage(dm, nw, sm, L.gate.type == 8 || L.up.type == 8);
-    for (int t = sg.a; t < sg.b; t += sg.per) {
-        const int k = min(sg.per, sg.b - t);
-        if (!unit_rows(L.gate, k, sm, rg, dm.err)) return false;
-        if (threadIdx.x < k * 8) sm.gate[(t - sg.a) * 8 + threadIdx.x] = sm.rows[threadIdx.x];
-        cons_sync();
-    }
+    norm_fold(dm, nw, sm, L.gate.type == 8 || L.up.type == 8);
+    const float nsc = norm_scale(dm, sm);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_GU);
-    for (int t = su.a; t < su.b; t += su.per) {
-        const int k = min(su.per, su.b - t);
-        if (!unit_rows(L.up, k, sm, rg, dm.err)) return false;
-        if (threadIdx.x < k * 8) {
-            const int row = t * 8 + threadIdx.x;
-            const float g = sm.gate[(t - su.a) * 8 + threadIdx.x], u = sm.rows[threadIdx.x];
-            if (row < dm.ff) {
-                const float den = __fadd_rn(1.f, (float)exp(-(double)g));
-                ll_put(dm.ll_act + row, __fmul_rn(__fdiv_rn(g, den), u), tag);
-            }
+    auto swiglu = [&](int row, float g, float u) {
+        if (row < dm.ff) {
+            const float den = __fadd_rn(1.f, (float)exp(-(double)g));  // as cpu.go:345
+            ll_put(dm.ll_act + row, __fmul_rn(__fdiv_rn(g, den), u), tag);
         }
+    };
+    if (gu_fused(L, sg, rg.slot_bytes)) {
+        const int n = sg.b - sg.a;
+        if (!unit_rows(L.gate, 2 * n, sm, rg, dm.err)) return false;
+        if (threadIdx.x < n * 8)
+            swiglu(sg.a * 8 + threadIdx.x, __fmul_rn(sm.rows[threadIdx.x], nsc),
+                   __fmul_rn(sm.rows[n * 8 + threadIdx.x], nsc));
         cons_sync();
+    } else {
+        for (int t = sg.a; t < sg.b; t += sg.per) {
+            const int k = min(sg.per, sg.b - t);
+            if (!unit_rows(L.gate, k, sm, rg, dm.err)) return false;
+            if (threadIdx.x < k * 8) sm.gate[(t - sg.a) * 8 + threadIdx.x] = __fmul_rn(sm.rows[threadIdx.x], nsc);
+            cons_sync();
+        }
+        for (int t = su.a; t < su.b; t += su.per) {
+            const int k = min(su.per, su.b - t);
+            if (!unit_rows(L.up, k, sm, rg, dm.err)) return false;
+            if (threadIdx.x < k * 8)
+                swiglu(t * 8 + threadIdx.x, sm.gate[(t - su.a) * 8 + threadIdx.x],
+                       __fmul_rn(sm.rows[threadIdx.x], nsc));
+            cons_sync();
+        }
     }
     tk.tr.stamp(ev, 2);
     return true;
@@ -959,13 +1026,14 @@ __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, R
         nw.load(dm.out_norm, E);
         if (cons_or(!poll_vec(dm.ll_x, E, tin, sm.xs, dm.err))) return false;
         tk.tr.stamp(ev, 1);
-        norm_stage(dm, nw, sm, dm.head.type == 8);
+        norm_fold(dm, nw, sm, dm.head.type == 8);
+        const float nsc = norm_scale(dm, sm);
         for (int t = s.a; t < s.b; t += s.per) {
             const int k = min(s.per, s.b - t);
             if (!unit_rows(dm.head, k, sm, rg, dm.err)) return false;
             if (threadIdx.x < k * 8) {
                 const int row = t * 8 + threadIdx.x;
-                const float v = sm.rows[threadIdx.x];
+                const float v = __fmul_rn(sm.rows[threadIdx.x], nsc);
                 if (row < dm.vocab) {
                     dm.logits[row] = v;
                     if (better(v, row, bv, bi)) bv = v, bi = row;
@@ -1083,7 +1151,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (!ph_qkv(dm, l, tk, sm, rg)) return;
             for (int item = blockIdx.x; item < dm.heads * nch; item += gridDim.x)
                 if (!ph_attn(dm, l, tk, item, nch, sm)) return;
-            if (!ph_o(dm, l, tk, nch, sm, rg)) return;
+            if (!ph_o(dm, l, tk, sm, rg)) return;
             if (!ph_gu(dm, l, tk, sm, rg)) return;
             if (!ph_down(dm, l, tk, sm, rg)) return;
         }

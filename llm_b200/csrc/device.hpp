@@ -84,7 +84,7 @@ struct ModelHeader {
     // optional phase timeline of the persistent decode kernel (null: off):
     // trace[(cta * trace_events + event) * 4 + {0, 1, 2}] = globaltimer ns at
     // the phase's entry, when its input was ready, at its exit, and + 3 the
-    // ns it waited for weight slots; events are
+    // SM cycles it waited for weight slots; events are
     // 5 per layer (QKV, attention, output, gate/up, down), then head, then
     // the token's grid barrier.  Recorded for the first token of a launch.
     uint64_t *trace;
@@ -130,7 +130,7 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     l.red = p, p += 4 * 64;
     l.att = p, p += 4 * (size_t)(3 * head_dim + 64) + 8 * 4 * 256;
     p = (p + 15) / 16 * 16;
-    l.merge = p, p += 4 * (size_t)(8 * embd + 8 * 2 * heads) + 8 * (size_t)(2 * heads + 9 * heads) + 16;
+    l.merge = p, p += 4 * (size_t)(9 * head_dim + 32);
     l.pre = p, p += 4 * (size_t)(3 * qkv_rows);
     p = (p + 127) / 128 * 128;
     l.kvs = p, p += 4 * (size_t)(2 * 64 * (head_dim + 16));
