@@ -40,7 +40,7 @@ constexpr int kConsThreads = kCons * 32; // 256
 constexpr int kDecThreads = kConsThreads + 32;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
 #ifndef LLMB_POLL_SLEEP_NS
-#define LLMB_POLL_SLEEP_NS 64
+#define LLMB_POLL_SLEEP_NS 0
 #endif
 constexpr unsigned kPollSleepNs = LLMB_POLL_SLEEP_NS;
 
@@ -125,9 +125,13 @@ struct Seg {
 };
 
 // Polls up to 3 tagged vectors.  Each consumer thread owns word pairs t,
-// t + 256, ... of their concatenation and issues the loads of up to 4 pairs
-// before testing any, so the vectors cost about one round trip per 1024
-// pairs, not one per value.
+// t + 256, ... of their concatenation.  It polls them in rounds of up to 4
+// pairs: every round issues the loads of all pairs still pending before
+// testing any, so once the data is written a thread sees all of it within
+// about one L2 round trip (a pair-by-pair wait would pay one round trip per
+// pair that was stale when loaded).  Without a back-off sleep a 576-float
+// vector written by 72 CTAs reaches all 148 CTAs in about 1.0 us on B200,
+// against 1.6 us with a 64 ns sleep.
 __device__ __forceinline__ const uint64_t *seg_src(const Seg *sg, int ns, int i, int &j, int &lo) {
     lo = 0;
     for (j = 0; j < ns; ++j) {
@@ -146,24 +150,35 @@ __device__ __noinline__ bool poll_segs(const Seg (&sg)[NS], int *err) {
     constexpr int K = 4;
     for (int base = 0; base < npairs; base += K * kConsThreads) {
         uint64_t v[2 * K];
+        unsigned pend = 0;
 #pragma unroll
-        for (int k = 0; k < K; ++k) {
-            int j, lo;
-            const uint64_t *p = seg_src(sg, NS, base + threadIdx.x + k * kConsThreads, j, lo);
-            if (p) ld_relaxed2(p, v[2 * k], v[2 * k + 1]);
-        }
+        for (int k = 0; k < K; ++k)
+            if (base + threadIdx.x + k * kConsThreads < npairs) pend |= 1u << k;
         const uint64_t t0 = gtimer();
         unsigned spins = 0;
+        while (pend) {
 #pragma unroll
-        for (int k = 0; k < K; ++k) {
-            const int i = base + threadIdx.x + k * kConsThreads;
-            int j, lo;
-            const uint64_t *p = seg_src(sg, NS, i, j, lo);
-            if (!p) continue;
-            const uint32_t tag = sg[j].tag;
-            while ((uint32_t)(v[2 * k] >> 32) != tag || (uint32_t)(v[2 * k + 1] >> 32) != tag) {
-                __nanosleep(kPollSleepNs);  // back off: every waiting thread polls the same few lines
-                ld_relaxed2(p, v[2 * k], v[2 * k + 1]);
+            for (int k = 0; k < K; ++k) {
+                if (!(pend >> k & 1)) continue;
+                int j, lo;
+                ld_relaxed2(seg_src(sg, NS, base + threadIdx.x + k * kConsThreads, j, lo), v[2 * k], v[2 * k + 1]);
+            }
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                if (!(pend >> k & 1)) continue;
+                const int i = base + threadIdx.x + k * kConsThreads;
+                int j, lo;
+                seg_src(sg, NS, i, j, lo);
+                const uint32_t tag = sg[j].tag;
+                if ((uint32_t)(v[2 * k] >> 32) == tag && (uint32_t)(v[2 * k + 1] >> 32) == tag) {
+                    float *d = sg[j].dst + 2 * (i - lo);
+                    d[0] = __uint_as_float((uint32_t)v[2 * k]);
+                    d[1] = __uint_as_float((uint32_t)v[2 * k + 1]);
+                    pend &= ~(1u << k);
+                }
+            }
+            if (pend) {
+                if (kPollSleepNs) __nanosleep(kPollSleepNs);
                 if ((++spins & 255) == 0) {
                     if (read_err(err)) return false;
                     if (gtimer() - t0 > kWaitNs) {
@@ -172,9 +187,6 @@ __device__ __noinline__ bool poll_segs(const Seg (&sg)[NS], int *err) {
                     }
                 }
             }
-            float *d = sg[j].dst + 2 * (i - lo);
-            d[0] = __uint_as_float((uint32_t)v[2 * k]);
-            d[1] = __uint_as_float((uint32_t)v[2 * k + 1]);
         }
     }
     return true;
