@@ -831,7 +831,7 @@ __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, i
         if (p < cnt) s = __fmul_rn(ps, dm.scale);
     }
     const float mx = cons_max(s, sm.red);
-    if (p < cnt && sub == 0) e[p] = (float)exp((double)__fsub_rn(s, mx));  // as cpu.go:321
+    if (p < cnt && sub == 0) e[p] = expf(__fsub_rn(s, mx));  // cpu.go:321 (exp in double there: within 2 ulp)
     cons_sync();
     constexpr int G = kConsThreads / V4;
     const int d4 = threadIdx.x % V4, g = threadIdx.x / V4;
@@ -852,14 +852,18 @@ __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, i
     part[threadIdx.x * 4 + 2] = o2, part[threadIdx.x * 4 + 3] = o3;
     cons_sync();
     float *own = sm.merge;  // the merging item's own partial: V sum [HD], max, sum of exp
+    float lsum = 0.f;
+    if (threadIdx.x < 32) {
+        lsum = (threadIdx.x < cnt ? e[threadIdx.x] : 0.f) + (threadIdx.x + 32 < cnt ? e[threadIdx.x + 32] : 0.f);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
+    }
     if (threadIdx.x < V4) {
         float t4[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int k = 0; k < G; ++k)
 #pragma unroll
             for (int j = 0; j < 4; ++j) t4[j] += part[(threadIdx.x + k * V4) * 4 + j];
-        float lsum = 0.f;
-        for (int pp = 0; pp < cnt; ++pp) lsum += e[pp];
         const size_t pi = (size_t)h * dm.nchunk + c;  // head-major: a head's chunks are contiguous
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
