@@ -2,15 +2,16 @@
 // in one cooperative launch over every SM (Generate's decode submits,
 // gpu.go:987-1009, and the per-token pass, gpu.go:792-832, fused.go:259-289).
 //
-// Structure of a CTA (one per SM):
-//   - a producer warp streams the CTA's weight tiles, in the order the CTA
-//     consumes them, through a ring of shared-memory slots with 1D bulk TMA
-//     copies (cp.async.bulk, no multicast) tracked by mbarriers.  Weights do
+// Structure of a CTA (one per SM, 8 warps, so up to 255 registers a thread):
+//   - the CTA's weight tiles stream, in the order the CTA consumes them,
+//     through a ring of shared-memory slots with 1D bulk TMA copies
+//     (cp.async.bulk, no multicast) tracked by mbarriers.  One thread issues
+//     them and refills each slot as soon as its unit is consumed.  Weights do
 //     not depend on activations, so the stream runs ahead across phases,
 //     layers and tokens as far as the ring allows;
-//   - 8 consumer warps compute.  Every tile's blocks are split across the
-//     warps (paired f32 math); the partials meet in shared memory and
-//     shuffles in a fixed order, so results are deterministic.
+//   - the 8 warps compute.  Every tile's blocks are split across the warps
+//     (paired f32 math); the partials meet in shared memory and shuffles in
+//     a fixed order, so results are deterministic.
 //
 // Activations move between CTAs as 64-bit words {f32 value, u32 tag}
 // written and polled with relaxed GPU-scope accesses (a value and its tag
@@ -21,8 +22,8 @@
 // publishes the argmax partials and the token's KV-cache rows.
 //
 // Every wait (mbarrier, tag poll, grid barrier) is bounded: past its limit
-// the kernel records an error in DevModel::err and returns; the producer
-// first waits (bounded) for its copies in flight.
+// the kernel records an error in DevModel::err and returns; the CTA first
+// waits (bounded) for its weight copies in flight.
 #include <cuda_fp16.h>
 
 #include <cfloat>
@@ -37,7 +38,8 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kCons = 8;                 // consumer warps
 constexpr int kConsThreads = kCons * 32; // 256
-constexpr int kDecThreads = kConsThreads + 32;
+constexpr int kDecThreads = kConsThreads;  // 8 warps: 2 per SM sub-partition, up to 255 registers each
+constexpr int kFeeder = kConsThreads - 1;  // the thread that issues the weight ring's copies
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
 #ifndef LLMB_POLL_SLEEP_NS
 #define LLMB_POLL_SLEEP_NS 0
@@ -68,10 +70,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *b, unsigned parity) {
         : "r"(smem_u32(b)), "r"(parity)
         : "memory");
     return ok != 0;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
-    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *b, unsigned bytes) {
@@ -290,7 +288,9 @@ __device__ __forceinline__ Share share(const QMat &m, int cta, int ncta, int slo
 // --------------------------------------------------------- smem layout --
 
 struct DecSmem {
-    uint64_t *full, *empty;  // ring mbarriers
+    uint64_t *full;          // ring mbarriers (one per slot)
+    struct Feed *feed;       // the feeder thread's cursor
+    FeedUnit *plan;          // the CTA's units of one token
     uint8_t *ring;           // nslots * slot_bytes
     float *xv;               // activation vector, paired layout for Q4 / plain for Q8 (max(E,F) floats)
     float *xq8;              // the same vector in plain layout when a Q8_0 matrix reads it
@@ -469,7 +469,7 @@ struct Ring {
 // The shared-memory views the tile pipeline needs (by value, so the
 // out-of-line unit_rows below takes no reference to kernel parameters).
 struct UnitCtx {
-    uint64_t *full, *empty;
+    uint64_t *full;
     uint8_t *ring;
     float *xv, *xq8, *part, *rows;
 };
@@ -512,7 +512,6 @@ __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const U
             if ((lane & 3) == 0) c.rows[i * 8 + (lane >> 2)] = a;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(c.empty + sl);
     } else {
         const int parts = kCons / k;
         const int tile = warp / parts, part = warp % parts;
@@ -522,7 +521,6 @@ __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const U
             a = dot_tile(m.type, slot + (size_t)tile * m.tile_bytes, m.nb, sm, b0, b1, lane);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(c.empty + sl);  // the slot is free once this warp's reads are done
         a += __shfl_xor_sync(kFull, a, 1);
         a += __shfl_xor_sync(kFull, a, 2);
         // partial of (row r, warp w) -> part[r * 8 + w]: the 8 parts of a row are 8 consecutive lanes
@@ -543,10 +541,14 @@ __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const U
     return true;
 }
 
-__device__ __forceinline__ bool unit_rows(const QMat &m, int k, const DecSmem &sm, Ring &rg, int *err) {
-    const UnitCtx c{sm.full, sm.empty, sm.ring, sm.xv, sm.xq8, reinterpret_cast<float *>(sm.part), sm.rows};
-    const bool ok = unit_rows_nl(m, k, c, rg.nslots, rg.slot_bytes, rg.u, err);
+__device__ __forceinline__ void feed_issue(const DecSmem &sm, int nslots, int slot_bytes);
+
+// One unit: its rows into sm.rows; then the feeder refills the slot it used.
+__device__ __forceinline__ bool unit_rows(const DecParams &dm, const QMat &m, int k, const DecSmem &sm, Ring &rg) {
+    const UnitCtx c{sm.full, sm.ring, sm.xv, sm.xq8, reinterpret_cast<float *>(sm.part), sm.rows};
+    const bool ok = unit_rows_nl(m, k, c, rg.nslots, rg.slot_bytes, rg.u, dm.err);
     rg.u++;
+    if (ok && threadIdx.x == kFeeder) feed_issue(sm, rg.nslots, rg.slot_bytes);
     return ok;
 }
 
@@ -559,114 +561,138 @@ __device__ __forceinline__ uint32_t tag_of(uint32_t epoch, int layers, int l, in
 
 enum { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4 };
 
-// ------------------------------------------------------------ producer --
-
-__device__ __forceinline__ bool prod_unit(const DecSmem &sm, int nslots, int slot_bytes, unsigned &u, const uint8_t *src,
-                                          unsigned bytes, int *err) {
-    const int slot = u % nslots;
-    const unsigned parity = ((u / nslots) & 1) ^ 1;
-    if (!mbar_try_wait(sm.empty + slot, parity)) {
-        const uint64_t t0 = gtimer();
-        while (!mbar_try_wait(sm.empty + slot, parity)) {
-            __nanosleep(256);  // the producer runs ahead: leave the scheduler to the consumer warps
-            if (read_err(err)) return false;
-            if (gtimer() - t0 > kWaitNs) {
-                atomicExch(err, DEV_RING_TIMEOUT);
-                return false;
-            }
-        }
-    }
-    mbar_expect_tx(sm.full + slot, bytes);
-    bulk_g2s(sm.ring + (size_t)slot * slot_bytes, src, bytes, sm.full + slot);
-    u++;
-    return true;
-}
-
 // Gate and up tiles of a CTA travel as one unit when they have one format and
-// fit one slot (the producer copies both ranges into the slot).
+// fit one slot (the feeder copies both ranges into the slot).
 __device__ __forceinline__ bool gu_fused(const Layer &L, const Share &sg, int slot_bytes) {
     const int n = sg.b - sg.a;
     return L.gate.type == L.up.type && L.gate.nb == L.up.nb && 2 * n * L.gate.tile_bytes <= slot_bytes &&
            2 * n <= kConsThreads / 8;
 }
 
-// One unit made of two ranges (gate tiles, then up tiles), one slot, one barrier.
-__device__ __forceinline__ bool prod_unit2(const DecSmem &sm, int nslots, int slot_bytes, unsigned &u,
-                                           const uint8_t *src1, unsigned bytes1, const uint8_t *src2, unsigned bytes2,
-                                           int *err) {
-    const int slot = u % nslots;
-    const unsigned parity = ((u / nslots) & 1) ^ 1;
-    if (!mbar_try_wait(sm.empty + slot, parity)) {
-        const uint64_t t0 = gtimer();
-        while (!mbar_try_wait(sm.empty + slot, parity)) {
-            __nanosleep(256);
-            if (read_err(err)) return false;
-            if (gtimer() - t0 > kWaitNs) {
-                atomicExch(err, DEV_RING_TIMEOUT);
-                return false;
-            }
-        }
-    }
-    mbar_expect_tx(sm.full + slot, bytes1 + bytes2);
-    bulk_g2s(sm.ring + (size_t)slot * slot_bytes, src1, bytes1, sm.full + slot);
-    bulk_g2s(sm.ring + (size_t)slot * slot_bytes + bytes1, src2, bytes2, sm.full + slot);
-    u++;
+// ------------------------------------------------------------- feeding --
+// The weight ring is filled by one consumer thread (kFeeder).  It issues the
+// CTA's units in the order the phases consume them: per token and layer the
+// QKV tiles one at a time, the output projection's share, gate and up (one
+// unit of two copies when gu_fused, else gate's share, then up's), down's
+// share; after the last layer the head's share.  A slot is refilled as soon
+// as the consumers have finished the unit in it, so the copies run nslots
+// units ahead of the consumers.  The sequence is the same for every token;
+// k_feed_plan lists it once per model (feed_next below), and the decode
+// kernel keeps the CTA's list in shared memory, so a refill is a few
+// instructions on the consumers' path.
+
+struct Feed {
+    int i, l, st, t;  // planning: token, layer, stage (0 QKV, 1 O, 2 gate or gate+up, 3 up, 4 down, 5 head), cursor
+    unsigned issued;  // units issued
+    int j, n;         // decoding: the next plan entry, entries per token
+    unsigned total;   // units of the launch
+};
+
+__device__ __forceinline__ bool share_unit(const QMat &m, const Share &s, int &ft, const uint8_t *&src, unsigned &n) {
+    const int t = s.a + ft;
+    if (t >= s.b) return false;
+    src = m.tiles + (size_t)t * m.tile_bytes;
+    n = (unsigned)(min(s.per, s.b - t) * m.tile_bytes);
+    ft += s.per;
     return true;
 }
 
-__device__ __forceinline__ bool prod_share(const DecSmem &sm, int nslots, int slot_bytes, unsigned &u, const QMat &m,
-                                           const Share &s, int *err) {
-    for (int t = s.a; t < s.b; t += s.per) {
-        const int k = min(s.per, s.b - t);
-        if (!prod_unit(sm, nslots, slot_bytes, u, m.tiles + (size_t)t * m.tile_bytes, (unsigned)(k * m.tile_bytes), err))
-            return false;
-    }
-    return true;
-}
-
-// The producer's stream: the same order as the consumers' phases.
-__device__ void producer(const DecParams &dm, const DecSmem &sm, int nslots, int slot_bytes, int ntok) {
-    if ((threadIdx.x & 31) != 0) return;
+// The next unit's one or two source ranges; false once the sequence is done.
+__device__ bool feed_next(const DecParams &dm, Feed &f, int ntok, int slot_bytes, const uint8_t *&s1, unsigned &n1,
+                          const uint8_t *&s2, unsigned &n2) {
     const int cta = blockIdx.x, ncta = gridDim.x;
-    unsigned u = 0;
-    bool ok = true;
-    for (int i = 0; i < ntok && ok; ++i) {
-        for (int l = 0; l < dm.layers && ok; ++l) {
-            const Layer &L = dm.layer[l];
-            const int nq = L.q.rows >> 3, nk = L.k.rows >> 3;
-            // QKV: one share over the concatenated tile index space
-            const int T = nq + nk + (L.v.rows >> 3);
+    n2 = 0;
+    while (f.i < ntok) {
+        if (f.st == 5) {
+            if (share_unit(dm.head, share(dm.head, cta, ncta, slot_bytes), f.t, s1, n1)) return true;
+            f.i++, f.l = 0, f.st = 0, f.t = 0;
+            continue;
+        }
+        const Layer &L = dm.layer[f.l];
+        if (f.st == 0) {
+            const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, T = nq + nk + (L.v.rows >> 3);
             const int P = min(ncta, T);
             if (cta < P) {
                 const int a = (int)((int64_t)T * cta / P), b = (int)((int64_t)T * (cta + 1) / P);
-                for (int t = a; t < b && ok; ++t) {
+                const int t = a + f.t;
+                if (t < b) {
                     const QMat &m = t < nq ? L.q : t < nq + nk ? L.k : L.v;
                     const int lt = t < nq ? t : t < nq + nk ? t - nq : t - nq - nk;
-                    ok = prod_unit(sm, nslots, slot_bytes, u, m.tiles + (size_t)lt * m.tile_bytes,
-                                   (unsigned)m.tile_bytes, dm.err);
+                    s1 = m.tiles + (size_t)lt * m.tile_bytes;
+                    n1 = (unsigned)m.tile_bytes;
+                    f.t++;
+                    return true;
                 }
             }
-            if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.o, share(L.o, cta, ncta, slot_bytes), dm.err);
+        } else if (f.st == 2) {
             const Share sg = share(L.gate, cta, ncta, slot_bytes);
-            if (ok && sg.b > sg.a && gu_fused(L, sg, slot_bytes)) {
-                const unsigned half = (unsigned)((sg.b - sg.a) * L.gate.tile_bytes);
-                ok = prod_unit2(sm, nslots, slot_bytes, u, L.gate.tiles + (size_t)sg.a * L.gate.tile_bytes, half,
-                                L.up.tiles + (size_t)sg.a * L.up.tile_bytes, half, dm.err);
-            } else {
-                if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.gate, sg, dm.err);
-                if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.up, share(L.up, cta, ncta, slot_bytes), dm.err);
+            if (sg.b > sg.a && gu_fused(L, sg, slot_bytes)) {
+                if (f.t == 0) {
+                    n1 = n2 = (unsigned)((sg.b - sg.a) * L.gate.tile_bytes);
+                    s1 = L.gate.tiles + (size_t)sg.a * L.gate.tile_bytes;
+                    s2 = L.up.tiles + (size_t)sg.a * L.up.tile_bytes;
+                    f.t = 1;
+                    return true;
+                }
+                f.st = 4, f.t = 0;  // up travelled with gate
+                continue;
             }
-            if (ok) ok = prod_share(sm, nslots, slot_bytes, u, L.down, share(L.down, cta, ncta, slot_bytes), dm.err);
+            if (share_unit(L.gate, sg, f.t, s1, n1)) return true;
+        } else {
+            const QMat &m = f.st == 1 ? L.o : f.st == 3 ? L.up : L.down;
+            if (share_unit(m, share(m, cta, ncta, slot_bytes), f.t, s1, n1)) return true;
         }
-        if (ok) ok = prod_share(sm, nslots, slot_bytes, u, dm.head, share(dm.head, cta, ncta, slot_bytes), dm.err);
+        f.t = 0;
+        if (f.st < 4) f.st++;
+        else if (f.l + 1 < dm.layers) f.l++, f.st = 0;
+        else f.st = 5;
     }
-    // drain: wait (bounded) for the copies still in flight before the CTA may exit
-    for (unsigned v = u > (unsigned)nslots ? u - nslots : 0; v < u; ++v) {
-        const int slot = v % nslots;
-        const unsigned parity = (v / nslots) & 1;
+    return false;
+}
+
+// Issues the next unit into the slot that follows the last one issued (the
+// caller guarantees the consumers are done with that slot).
+__device__ __forceinline__ void feed_issue(const DecSmem &sm, int nslots, int slot_bytes) {
+    Feed &f = *sm.feed;
+    if (f.issued >= f.total) return;
+    const FeedUnit e = sm.plan[f.j];
+    f.j = f.j + 1 == f.n ? 0 : f.j + 1;
+    const int slot = f.issued % (unsigned)nslots;
+    uint8_t *dst = sm.ring + (size_t)slot * slot_bytes;
+    // the slot's previous contents were read through the generic proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(sm.full + slot, e.n1 + e.n2);
+    bulk_g2s(dst, e.src1, e.n1, sm.full + slot);
+    if (e.n2) bulk_g2s(dst + e.n1, e.src2, e.n2, sm.full + slot);
+    f.issued++;
+}
+
+// Lists each CTA's units of one token (one thread per CTA, the decode
+// kernel's grid); count -1 if they exceed kMaxFeedPlan.
+__global__ void k_feed_plan(const __grid_constant__ DecParams dm, int slot_bytes, FeedUnit *plan, int *count) {
+    if (threadIdx.x != 0) return;
+    Feed f{};
+    FeedUnit *out = plan + (size_t)blockIdx.x * kMaxFeedPlan;
+    const uint8_t *s1, *s2;
+    unsigned n1, n2;
+    int n = 0;
+    while (feed_next(dm, f, 1, slot_bytes, s1, n1, s2, n2)) {
+        if (n == kMaxFeedPlan) {
+            count[blockIdx.x] = -1;
+            return;
+        }
+        out[n++] = FeedUnit{s1, n2 ? s2 : nullptr, n1, n2};
+    }
+    count[blockIdx.x] = n;
+}
+
+// Before the CTA exits: waits (bounded) for the copies issued but not consumed
+// (only an error path leaves any).
+__device__ void feed_drain(const DecSmem &sm, int nslots, unsigned consumed) {
+    for (unsigned v = consumed; v < sm.feed->issued; ++v) {
         const uint64_t t0 = gtimer();
-        while (!mbar_try_wait(sm.full + slot, parity))
-            if (gtimer() - t0 > kWaitNs) break;
+        while (!mbar_try_wait(sm.full + v % nslots, (v / nslots) & 1))
+            if (gtimer() - t0 > kWaitNs / 4) break;
     }
 }
 
@@ -730,7 +756,7 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
         const int seg = t < nq ? 0 : t < nq + nk ? 1 : 2;
         const QMat &m = seg == 0 ? L.q : seg == 1 ? L.k : L.v;
         const int lt = seg == 0 ? t : seg == 1 ? t - nq : t - nq - nk;
-        if (!unit_rows(m, 1, sm, rg, dm.err)) return false;
+        if (!unit_rows(dm, m, 1, sm, rg)) return false;
         if (threadIdx.x < 8) {
             const int r = threadIdx.x, row = lt * 8 + r;
             const float *pre = sm.pre + 3 * ((t - a) * 8);
@@ -940,7 +966,7 @@ __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &s
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_O);
     for (int t = s.a; t < s.b; t += s.per) {
         const int k = min(s.per, s.b - t);
-        if (!unit_rows(L.o, k, sm, rg, dm.err)) return false;
+        if (!unit_rows(dm, L.o, k, sm, rg)) return false;
         if (threadIdx.x < k * 8) {
             const int row = t * 8 + threadIdx.x;
             ll_put(dm.ll_x + row, __fadd_rn(sm.gate[row - s.a * 8], sm.rows[threadIdx.x]), tag);
@@ -975,7 +1001,7 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     };
     if (gu_fused(L, sg, rg.slot_bytes)) {
         const int n = sg.b - sg.a;
-        if (!unit_rows(L.gate, 2 * n, sm, rg, dm.err)) return false;
+        if (!unit_rows(dm, L.gate, 2 * n, sm, rg)) return false;
         if (threadIdx.x < n * 8)
             swiglu(sg.a * 8 + threadIdx.x, __fmul_rn(sm.rows[threadIdx.x], nsc),
                    __fmul_rn(sm.rows[n * 8 + threadIdx.x], nsc));
@@ -983,13 +1009,13 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     } else {
         for (int t = sg.a; t < sg.b; t += sg.per) {
             const int k = min(sg.per, sg.b - t);
-            if (!unit_rows(L.gate, k, sm, rg, dm.err)) return false;
+            if (!unit_rows(dm, L.gate, k, sm, rg)) return false;
             if (threadIdx.x < k * 8) sm.gate[(t - sg.a) * 8 + threadIdx.x] = __fmul_rn(sm.rows[threadIdx.x], nsc);
             cons_sync();
         }
         for (int t = su.a; t < su.b; t += su.per) {
             const int k = min(su.per, su.b - t);
-            if (!unit_rows(L.up, k, sm, rg, dm.err)) return false;
+            if (!unit_rows(dm, L.up, k, sm, rg)) return false;
             if (threadIdx.x < k * 8)
                 swiglu(t * 8 + threadIdx.x, sm.gate[(t - su.a) * 8 + threadIdx.x],
                        __fmul_rn(sm.rows[threadIdx.x], nsc));
@@ -1017,7 +1043,7 @@ __device__ bool ph_down(const DecParams &dm, int l, const Tok &tk, const DecSmem
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_DOWN);
     for (int t = s.a; t < s.b; t += s.per) {
         const int k = min(s.per, s.b - t);
-        if (!unit_rows(L.down, k, sm, rg, dm.err)) return false;
+        if (!unit_rows(dm, L.down, k, sm, rg)) return false;
         if (threadIdx.x < k * 8) {
             const int row = t * 8 + threadIdx.x;
             ll_put(dm.ll_x + row, __fadd_rn(sm.gate[row - s.a * 8], sm.rows[threadIdx.x]), tag);
@@ -1046,7 +1072,7 @@ __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, R
         const float nsc = norm_scale(dm, sm);
         for (int t = s.a; t < s.b; t += s.per) {
             const int k = min(s.per, s.b - t);
-            if (!unit_rows(dm.head, k, sm, rg, dm.err)) return false;
+            if (!unit_rows(dm, dm.head, k, sm, rg)) return false;
             if (threadIdx.x < k * 8) {
                 const int row = t * 8 + threadIdx.x;
                 const float v = __fmul_rn(sm.rows[threadIdx.x], nsc);
@@ -1107,38 +1133,10 @@ __device__ int final_argmax(const DecParams &dm, const DecSmem &sm) {
     return __float_as_int(sm.red[2 * kCons]);
 }
 
-__global__ void __launch_bounds__(kDecThreads, 1)
-    k_decode2(const __grid_constant__ DecParams dm, GridBarrier *bar, int ntok, int nslots, int slot_bytes) {
-    extern __shared__ __align__(128) uint8_t dsm[];
-    DecSmem sm;
-    {
-        const DecLayout lo =
-            dec_layout(nslots, slot_bytes, dm.embd, dm.ff, dm.head_dim, dm.heads, dm.dec_gate_rows, dm.dec_qkv_rows);
-        sm.ring = dsm + lo.ring;
-        sm.full = reinterpret_cast<uint64_t *>(dsm + lo.full);
-        sm.empty = reinterpret_cast<uint64_t *>(dsm + lo.empty);
-        sm.xv = reinterpret_cast<float *>(dsm + lo.xv);
-        sm.xq8 = reinterpret_cast<float *>(dsm + lo.xq8);
-        sm.xs = reinterpret_cast<float *>(dsm + lo.xs);
-        sm.part = reinterpret_cast<double *>(dsm + lo.part);
-        sm.rows = reinterpret_cast<float *>(dsm + lo.rows);
-        sm.gate = reinterpret_cast<float *>(dsm + lo.gate);
-        sm.red = reinterpret_cast<float *>(dsm + lo.red);
-        sm.att = reinterpret_cast<float *>(dsm + lo.att);
-        sm.merge = reinterpret_cast<float *>(dsm + lo.merge);
-        sm.pre = reinterpret_cast<float *>(dsm + lo.pre);
-        sm.kvs = reinterpret_cast<float *>(dsm + lo.kvs);
-    }
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < nslots; ++i) mbar_init(sm.full + i, 1), mbar_init(sm.empty + i, kCons);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    if (threadIdx.x >= kConsThreads) {
-        producer(dm, sm, nslots, slot_bytes, ntok);
-        return;
-    }
-    Ring rg{nslots, slot_bytes, 0u};
+// The token loop of the persistent kernel (returns early on a device error,
+// which dm.err records).
+__device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *bar, int ntok, const DecSmem &sm,
+                                              Ring &rg) {
     Tok tk;
     tk.pos = (int)__ldcg(dm.state), tk.step = (int)__ldcg(dm.state + 1);
     tk.tok = __ldcg(dm.tokens + tk.step);
@@ -1187,22 +1185,62 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
 }
 
+__global__ void __launch_bounds__(kDecThreads, 1)
+    k_decode2(const __grid_constant__ DecParams dm, GridBarrier *bar, int ntok, int nslots, int slot_bytes) {
+    extern __shared__ __align__(128) uint8_t dsm[];
+    DecSmem sm;
+    {
+        const DecLayout lo =
+            dec_layout(nslots, slot_bytes, dm.embd, dm.ff, dm.head_dim, dm.heads, dm.dec_gate_rows, dm.dec_qkv_rows,
+                       dm.feed_max);
+        sm.ring = dsm + lo.ring;
+        sm.full = reinterpret_cast<uint64_t *>(dsm + lo.full);
+        sm.feed = reinterpret_cast<Feed *>(dsm + lo.feed);
+        sm.plan = reinterpret_cast<FeedUnit *>(dsm + lo.plan);
+        sm.xv = reinterpret_cast<float *>(dsm + lo.xv);
+        sm.xq8 = reinterpret_cast<float *>(dsm + lo.xq8);
+        sm.xs = reinterpret_cast<float *>(dsm + lo.xs);
+        sm.part = reinterpret_cast<double *>(dsm + lo.part);
+        sm.rows = reinterpret_cast<float *>(dsm + lo.rows);
+        sm.gate = reinterpret_cast<float *>(dsm + lo.gate);
+        sm.red = reinterpret_cast<float *>(dsm + lo.red);
+        sm.att = reinterpret_cast<float *>(dsm + lo.att);
+        sm.merge = reinterpret_cast<float *>(dsm + lo.merge);
+        sm.pre = reinterpret_cast<float *>(dsm + lo.pre);
+        sm.kvs = reinterpret_cast<float *>(dsm + lo.kvs);
+    }
+    const int nplan = __ldg(dm.feed_count + blockIdx.x);
+    for (int j = threadIdx.x; j < nplan; j += kConsThreads)
+        sm.plan[j] = dm.feed_plan[(size_t)blockIdx.x * kMaxFeedPlan + j];
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nslots; ++i) mbar_init(sm.full + i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        *sm.feed = Feed{0, 0, 0, 0, 0u, 0, nplan, (unsigned)(ntok * nplan)};
+    }
+    __syncthreads();
+    if (threadIdx.x == kFeeder)
+        for (int i = 0; i < nslots; ++i) feed_issue(sm, nslots, slot_bytes);
+    Ring rg{nslots, slot_bytes, 0u};
+    decode_tokens(dm, bar, ntok, sm, rg);
+    if (threadIdx.x == kFeeder) feed_drain(sm, nslots, rg.u);
+}
+
 }  // namespace
 
-DecConfig decode_config(const Shapes &s, int max_tile_bytes, int gate_rows, int qkv_rows) {
+DecConfig decode_config(const Shapes &s, int max_tile_bytes, int gate_rows, int qkv_rows, int plan_units) {
     // A ring of 4 slots of at least 16 KB: it runs far enough ahead of the
     // consumers, and a block of well under the 227 KB opt-in maximum leaves
     // the SM most of its L1, which holds the threads' stack and the norm and
     // RoPE rows each phase reads (with the maximum, this kernel ran 5 % slower).
     DecConfig c{};
     const int budget = 232448 - 8192;  // the opt-in maximum per block, less margin
-    DecLayout base = dec_layout(0, 0, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows);
+    DecLayout base = dec_layout(0, 0, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows, plan_units);
     const int ring = budget - (int)base.total;
     int slot = max(max_tile_bytes, 16384);
     slot = (slot + 127) / 128 * 128;
     c.slot_bytes = slot;
     c.nslots = min(4, ring / slot);
-    c.smem = dec_layout(c.nslots, c.slot_bytes, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows).total;
+    c.smem = dec_layout(c.nslots, c.slot_bytes, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows, plan_units).total;
     c.threads = kDecThreads;
     return c;
 }
@@ -1222,6 +1260,12 @@ cudaError_t launch_decode2(const DecParams &dm, const DecConfig &c, GridBarrier 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, k_decode2, dm, bar, ntok, c.nslots, c.slot_bytes);
+}
+
+cudaError_t launch_feed_plan(const DecParams &dm, int slot_bytes, FeedUnit *plan, int *count, int ctas,
+                             cudaStream_t st) {
+    k_feed_plan<<<ctas, 32, 0, st>>>(dm, slot_bytes, plan, count);
+    return cudaGetLastError();
 }
 
 int decode2_ctas_per_sm(const DecConfig &c) {

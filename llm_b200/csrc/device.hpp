@@ -50,6 +50,14 @@ struct Layer {
 };
 
 // What the kernels need besides the per-layer descriptors.
+// One unit of a CTA's weight stream in the persistent decode kernel: one or
+// two source ranges copied into one ring slot.
+struct FeedUnit {
+    const uint8_t *src1, *src2;
+    uint32_t n1, n2;
+};
+constexpr int kMaxFeedPlan = 1024;  // units of one token per CTA
+
 struct ModelHeader {
     int embd, ff, heads, kv_heads, head_dim, kvd, vocab, ctx, layers;
     float eps, scale;  // RMSNorm epsilon; 1/sqrt(head_dim) (cpu.go:304)
@@ -81,6 +89,11 @@ struct ModelHeader {
     uint32_t *ll_epoch;  // tokens decoded so far by the persistent kernel (makes tags unique across calls)
     int dec_gate_rows;   // gate rows of the largest gate/up share of a CTA
     int dec_qkv_rows;    // rows of the largest QKV share of a CTA
+    // each CTA's units of one token, in consumption order (plan[cta * kMaxFeedPlan + j],
+    // feed_count[cta] of them; feed_max the largest count), built once per model
+    const FeedUnit *feed_plan;
+    const int *feed_count;
+    int feed_max;
     // optional phase timeline of the persistent decode kernel (null: off):
     // trace[(cta * trace_events + event) * 4 + {0, 1, 2}] = globaltimer ns at
     // the phase's entry, when its input was ready, at its exit, and + 3 the
@@ -108,17 +121,18 @@ static_assert(sizeof(DecParams) < 32000, "kernel parameters are limited to 32 KB
 
 // Shared-memory layout of the persistent decode kernel (byte offsets).
 struct DecLayout {
-    size_t ring, full, empty, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, total;
+    size_t ring, full, feed, plan, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, total;
 };
 
 __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int embd, int ff, int head_dim, int heads,
-                                                int gate_rows, int qkv_rows) {
+                                                int gate_rows, int qkv_rows, int plan_units) {
     DecLayout l{};
     const size_t vec = (size_t)(embd > ff ? embd : ff) * 4;
     size_t p = 0;
     l.ring = p, p += (size_t)nslots * slot_bytes;
     l.full = p, p += 8 * (size_t)nslots;
-    l.empty = p, p += 8 * (size_t)nslots;
+    l.feed = p, p += 32;
+    l.plan = p, p += sizeof(FeedUnit) * (size_t)plan_units;
     p = (p + 127) / 128 * 128;
     l.xv = p, p += vec;
     l.xq8 = p, p += vec;

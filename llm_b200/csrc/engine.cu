@@ -230,6 +230,17 @@ struct Loader {
     }
 };
 
+
+// The largest tile (bytes) of the head and the layers' matrices.
+static int max_tile_of(const DevModel &d, int layers) {
+    int t = d.head.tile_bytes;
+    for (int l = 0; l < layers; l++) {
+        const Layer &L = d.layer[l];
+        for (const QMat *q : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) t = std::max(t, q->tile_bytes);
+    }
+    return t;
+}
+
 Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     GgufFile f;
     std::string msg;
@@ -363,11 +374,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
         !(d.trace = m.alloc<uint64_t>((size_t)m.persistent_ctas * d.trace_events * 4 * 8, err)))
         return err;
     {
-        int max_tile = d.head.tile_bytes;
-        for (int l = 0; l < c.layers; l++) {
-            const Layer &L = d.layer[l];
-            for (const QMat *q : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) max_tile = std::max(max_tile, q->tile_bytes);
-        }
+        const int max_tile = max_tile_of(d, c.layers);
         const int T = F / 8, P = std::min(m.persistent_ctas, T);
         d.dec_gate_rows = (T + P - 1) / P * 8;
         const int Tq = (E + 2 * kvd) / 8, Pq = std::min(m.persistent_ctas, Tq);
@@ -378,17 +385,40 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
         if (E > 1024) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports embedding sizes up to 1024"};
         if (c.head_dim != 64 && c.head_dim != 128)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel supports head sizes 64 and 128"};
-        m.dec = decode_config(s, max_tile, d.dec_gate_rows, d.dec_qkv_rows);
+        m.dec = decode_config(s, max_tile, d.dec_gate_rows, d.dec_qkv_rows, 0);
         if (c.layers > kMaxDecLayers) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports up to 64 layers"};
         if (m.dec.nslots < 2 || decode2_ctas_per_sm(m.dec) < 1)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel does not fit an SM (tiles of " + std::to_string(max_tile) +
                                          " bytes)"};
     }
+    FeedUnit *plan = nullptr;
+    int *plan_count = nullptr;
+    if (!(plan = m.alloc<FeedUnit>((size_t)m.persistent_ctas * kMaxFeedPlan * sizeof(FeedUnit), err))) return err;
+    if (!(plan_count = m.alloc<int>((size_t)m.persistent_ctas * 4, err))) return err;
+    d.feed_plan = plan, d.feed_count = plan_count;
     if (!(m.dm = m.alloc<DevModel>(sizeof(DevModel), err))) return err;
     CUDA_TRY(cudaMemcpyAsync(m.dm, &d, sizeof(DevModel), cudaMemcpyHostToDevice, m.st));
     m.dp = std::make_unique<DecParams>();
     static_cast<ModelHeader &>(*m.dp) = static_cast<const ModelHeader &>(d);
     for (int l = 0; l < c.layers; l++) m.dp->layer[l] = d.layer[l];
+    {
+        // the persistent kernel's weight stream, listed once: its length per CTA sizes the kernel's shared memory
+        CUDA_TRY(launch_feed_plan(*m.dp, m.dec.slot_bytes, plan, plan_count, m.persistent_ctas, m.st));
+        std::vector<int> counts(m.persistent_ctas);
+        CUDA_TRY(cudaMemcpyAsync(counts.data(), plan_count, counts.size() * 4, cudaMemcpyDeviceToHost, m.st));
+        CUDA_TRY(cudaStreamSynchronize(m.st));
+        int mx = 0;
+        for (int v : counts) {
+            if (v < 0) return {LLMB_ERR_CONFIG, "llm: the decode kernel's weight stream exceeds its plan"};
+            mx = std::max(mx, v);
+        }
+        m.dp->feed_max = mx;
+        const DecConfig full = decode_config(s, max_tile_of(d, c.layers), d.dec_gate_rows, d.dec_qkv_rows, mx);
+        if (full.nslots != m.dec.nslots || full.slot_bytes != m.dec.slot_bytes || full.smem > 232448 ||
+            decode2_ctas_per_sm(full) < 1)
+            return {LLMB_ERR_CONFIG, "llm: the decode kernel does not fit an SM with its weight plan"};
+        m.dec = full;
+    }
     CUDA_TRY(cudaHostAlloc(&m.h_tokens, (size_t)(ctx + 2 * kMaxDecodeBatch + 1) * 4, cudaHostAllocDefault));
     CUDA_TRY(cudaHostAlloc(&m.h_state, 16, cudaHostAllocDefault));
     CUDA_TRY(cudaHostAlloc(&m.h_err, 4, cudaHostAllocDefault));
