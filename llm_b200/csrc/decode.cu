@@ -303,6 +303,7 @@ struct DecSmem {
     float *merge;            // attention partials of up to 8 chunks: pv [8][E], then (max, sum) [8][H]
     float *pre;              // the QKV epilogue's bias and RoPE (cos, sin) per row of the CTA's share
     float *kvs;              // an attention item's history K and V rows [2][kAttnChunk][head_dim]
+    float *nrm;              // the next norm's weights (embd floats)
 };
 
 // --------------------------------------------------------- dot products --
@@ -408,18 +409,28 @@ __device__ __forceinline__ float cons_max(float v, float *red) {
     return t;
 }
 
-// A consumer thread's norm weights (elements t, t + 256, ..., embd <= 1024),
-// loaded before the phase waits for its input, off the critical path.
-struct NormW {
-    float w[4];
-    __device__ void load(const float *wp, int E) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int i = threadIdx.x + k * kConsThreads;
-            w[k] = i < E ? __ldg(wp + i) : 0.f;
-        }
-    }
-};
+// Asynchronous global -> shared copies (cp.async): the issuing thread does not
+// wait for them; cp_async_wait_all waits for all of the thread's copies.
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
+
+// Norm weights into sm.nrm (embd is a multiple of 32, the weights 256-byte
+// aligned), issued at the start of the phase before the one that uses them:
+// the copies complete while that phase runs, off the path from the input's
+// arrival to the first dot product.  norm_fold waits for them.
+__device__ __forceinline__ void prefetch_norm(const float *w, int E, const DecSmem &sm) {
+    for (int i = threadIdx.x; 4 * i < E; i += kConsThreads) cp_async16(sm.nrm + 4 * i, w + 4 * i);
+}
 
 // RMSNorm (cpu.go:81-98), folded: stages x * w (into the layouts the dot
 // products read) and leaves the warps' partial sums of squares in red[32..39];
@@ -427,8 +438,10 @@ struct NormW {
 // instead of every element, which keeps the sum of squares, the division and
 // the square root off the path to the first dot product.  (x * w) * s and
 // cpu.go's (x * s) * w differ only in rounding.
-__device__ __forceinline__ void norm_fold(const DecParams &dm, const NormW &nw, const DecSmem &sm, bool q8) {
+__device__ __forceinline__ void norm_fold(const DecParams &dm, const DecSmem &sm, bool q8) {
     const int E = dm.embd;
+    cp_async_wait_all();  // this thread's prefetches (norm weights, QKV epilogue inputs), then everyone's
+    cons_sync();
     float ss = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -436,7 +449,7 @@ __device__ __forceinline__ void norm_fold(const DecParams &dm, const NormW &nw, 
         if (i >= E) break;
         const float x = sm.xs[i];
         ss = fmaf(x, x, ss);
-        const float v = __fmul_rn(x, nw.w[k]);
+        const float v = __fmul_rn(x, sm.nrm[i]);
         const int b = i >> 5, j = i & 31, pj = j & 15;
         sm.xv[b * 32 + 2 * pj + (j >> 4)] = v;
         if (q8) sm.xq8[i] = v;
@@ -707,6 +720,33 @@ struct Tok {
 };
 
 // K1: RMSNorm + QKV + bias + RoPE + KV append (kernels_fused.go:47-73).
+// The QKV epilogue's inputs that do not depend on the token's activations
+// (bias, RoPE cos and sin of the position), and the attention norm's weights:
+// issued before the previous layer's down projection.
+__device__ __forceinline__ void qkv_prefetch(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm) {
+    const Layer &L = dm.layer[l];
+    const int cta = blockIdx.x, ncta = gridDim.x;
+    const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, T = nq + nk + (L.v.rows >> 3);
+    const int P = min(ncta, T);
+    if (cta >= P) return;
+    prefetch_norm(L.attn_norm, dm.embd, sm);
+    const int a = (int)((int64_t)T * cta / P), b = (int)((int64_t)T * (cta + 1) / P);
+    const int hp = dm.head_dim >> 1;
+    for (int i = threadIdx.x; i < (b - a) * 8; i += kConsThreads) {
+        const int t = a + (i >> 3), r = i & 7;
+        const int seg = t < nq ? 0 : t < nq + nk ? 1 : 2;
+        const int row = (seg == 0 ? t : seg == 1 ? t - nq : t - nq - nk) * 8 + r;
+        const float *bias = seg == 0 ? L.bq : seg == 1 ? L.bk : L.bv;
+        if (bias) cp_async4(sm.pre + 4 * i, bias + row);
+        else sm.pre[4 * i] = 0.f;
+        if (seg < 2)
+            cp_async8(sm.pre + 4 * i + 2, reinterpret_cast<const float2 *>(dm.rope_cs) + (size_t)tk.pos * hp +
+                                              ((row % dm.head_dim) >> 1));
+        else
+            sm.pre[4 * i + 2] = 1.f, sm.pre[4 * i + 3] = 0.f;
+    }
+}
+
 __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Layer &L = dm.layer[l];
     const int cta = blockIdx.x, ncta = gridDim.x;
@@ -717,20 +757,6 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
     tk.tr.stamp(ev, 0);
     const uint32_t tag_in = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
     const int a = (int)((int64_t)T * cta / P), b = (int)((int64_t)T * (cta + 1) / P);
-    const int hp = dm.head_dim >> 1;
-    NormW nw;
-    nw.load(L.attn_norm, E);
-    // the epilogue's inputs that do not depend on the token's activations
-    for (int i = threadIdx.x; i < (b - a) * 8; i += kConsThreads) {
-        const int t = a + (i >> 3), r = i & 7;
-        const int seg = t < nq ? 0 : t < nq + nk ? 1 : 2;
-        const int row = (seg == 0 ? t : seg == 1 ? t - nq : t - nq - nk) * 8 + r;
-        const float *bias = seg == 0 ? L.bq : seg == 1 ? L.bk : L.bv;
-        sm.pre[3 * i] = bias ? __ldg(bias + row) : 0.f;
-        float2 cs = make_float2(1.f, 0.f);
-        if (seg < 2) cs = __ldg(reinterpret_cast<const float2 *>(dm.rope_cs) + (size_t)tk.pos * hp + ((row % dm.head_dim) >> 1));
-        sm.pre[3 * i + 1] = cs.x, sm.pre[3 * i + 2] = cs.y;
-    }
     if (l == 0) {
         for (int e = threadIdx.x; e < E; e += kConsThreads) {
             const QMat &m = dm.embed;
@@ -749,7 +775,7 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
     }
     tk.tr.stamp(ev, 1);
     const bool q8 = L.q.type == 8 || L.k.type == 8 || L.v.type == 8;
-    norm_fold(dm, nw, sm, q8);
+    norm_fold(dm, sm, q8);
     const float nsc = norm_scale(dm, sm);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
     for (int t = a; t < b; ++t) {
@@ -759,14 +785,14 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
         if (!unit_rows(dm, m, 1, sm, rg)) return false;
         if (threadIdx.x < 8) {
             const int r = threadIdx.x, row = lt * 8 + r;
-            const float *pre = sm.pre + 3 * ((t - a) * 8);
+            const float *pre = sm.pre + 4 * ((t - a) * 8);
             const bool has_bias = (seg == 0 ? L.bq : seg == 1 ? L.bk : L.bv) != nullptr;
             float v = __fmul_rn(sm.rows[r], nsc);
-            if (has_bias) v = __fadd_rn(v, pre[3 * r]);
+            if (has_bias) v = __fadd_rn(v, pre[4 * r]);
             if (seg < 2) {
                 float o = __fmul_rn(sm.rows[r ^ 1], nsc);
-                if (has_bias) o = __fadd_rn(o, pre[3 * (r ^ 1)]);
-                const float2 cs = make_float2(pre[3 * r + 1], pre[3 * r + 2]);
+                if (has_bias) o = __fadd_rn(o, pre[4 * (r ^ 1)]);
+                const float2 cs = make_float2(pre[4 * r + 2], pre[4 * r + 3]);
                 if ((r & 1) == 0) v = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(o, cs.y));
                 else v = __fadd_rn(__fmul_rn(o, cs.y), __fmul_rn(v, cs.x));
             }
@@ -784,13 +810,6 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
     }
     tk.tr.stamp(ev, 2);
     return true;
-}
-
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
 }
 
 // K2: attention of the token (n = pos + 1 positions) for item (head,
@@ -825,9 +844,10 @@ __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, i
         cp_async16(ks + p * KS + d4 * 4, L.kv + row);
         cp_async16(vs + p * KS + d4 * 4, L.kv + (size_t)dm.ctx * dm.kvd + row);
     }
-    const bool ok = poll_two(dm.ll_q + h * HD, HD, tag, qh, has_cur ? dm.ll_k + kvh * HD : nullptr, has_cur ? HD : 0,
-                             tag, kc, dm.err) &&
-                    (!has_cur || poll_vec(dm.ll_v + kvh * HD, HD, tag, vc, dm.err));
+    const int ncur = has_cur ? HD : 0;
+    const Seg qkv[3] = {{dm.ll_q + h * HD, HD, tag, qh}, {dm.ll_k + kvh * HD, ncur, tag, kc},
+                        {dm.ll_v + kvh * HD, ncur, tag, vc}};
+    const bool ok = poll_segs(qkv, dm.err);
     cp_async_wait_all();
     if (cons_or(!ok)) return false;
     tk.tr.stamp(ev, 1);
@@ -986,11 +1006,9 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     const int E = dm.embd, ev = l * 5 + PH_GU;
     tk.tr.stamp(ev, 0);
     const uint32_t tin = tag_of(tk.epoch, dm.layers, l, PH_O);
-    NormW nw;
-    nw.load(L.ffn_norm, E);
     if (cons_or(!poll_vec(dm.ll_x, E, tin, sm.xs, dm.err))) return false;
     tk.tr.stamp(ev, 1);
-    norm_fold(dm, nw, sm, L.gate.type == 8 || L.up.type == 8);
+    norm_fold(dm, sm, L.gate.type == 8 || L.up.type == 8);
     const float nsc = norm_scale(dm, sm);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_GU);
     auto swiglu = [&](int row, float g, float u) {
@@ -1064,11 +1082,9 @@ __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, R
     if (s.b > s.a) {
         const int E = dm.embd;
         const uint32_t tin = tag_of(tk.epoch, dm.layers, dm.layers - 1, PH_DOWN);
-        NormW nw;
-        nw.load(dm.out_norm, E);
         if (cons_or(!poll_vec(dm.ll_x, E, tin, sm.xs, dm.err))) return false;
         tk.tr.stamp(ev, 1);
-        norm_fold(dm, nw, sm, dm.head.type == 8);
+        norm_fold(dm, sm, dm.head.type == 8);
         const float nsc = norm_scale(dm, sm);
         for (int t = s.a; t < s.b; t += s.per) {
             const int k = min(s.per, s.b - t);
@@ -1161,12 +1177,16 @@ __device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *
                 ll_put(dm.ll_x + e, v, tag_of(tk.epoch, dm.layers, -1, PH_DOWN));
             }
         }
+        qkv_prefetch(dm, 0, tk, sm);
         for (int l = 0; l < dm.layers; ++l) {
             if (!ph_qkv(dm, l, tk, sm, rg)) return;
             for (int item = blockIdx.x; item < dm.heads * nch; item += gridDim.x)
                 if (!ph_attn(dm, l, tk, item, nch, sm)) return;
+            prefetch_norm(dm.layer[l].ffn_norm, dm.embd, sm);
             if (!ph_o(dm, l, tk, sm, rg)) return;
             if (!ph_gu(dm, l, tk, sm, rg)) return;
+            if (l + 1 < dm.layers) qkv_prefetch(dm, l + 1, tk, sm);
+            else prefetch_norm(dm.out_norm, dm.embd, sm);
             if (!ph_down(dm, l, tk, sm, rg)) return;
         }
         if (!ph_head(dm, tk, sm, rg)) return;
@@ -1208,6 +1228,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         sm.merge = reinterpret_cast<float *>(dsm + lo.merge);
         sm.pre = reinterpret_cast<float *>(dsm + lo.pre);
         sm.kvs = reinterpret_cast<float *>(dsm + lo.kvs);
+        sm.nrm = reinterpret_cast<float *>(dsm + lo.nrm);
     }
     const int nplan = __ldg(dm.feed_count + blockIdx.x);
     for (int j = threadIdx.x; j < nplan; j += kConsThreads)

@@ -121,7 +121,7 @@ static_assert(sizeof(DecParams) < 32000, "kernel parameters are limited to 32 KB
 
 // Shared-memory layout of the persistent decode kernel (byte offsets).
 struct DecLayout {
-    size_t ring, full, feed, plan, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, total;
+    size_t ring, full, feed, plan, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, nrm, total;
 };
 
 __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int embd, int ff, int head_dim, int heads,
@@ -145,9 +145,11 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     l.att = p, p += 4 * (size_t)(3 * head_dim + 64) + 8 * 4 * 256;
     p = (p + 15) / 16 * 16;
     l.merge = p, p += 4 * (size_t)(9 * head_dim + 32);
-    l.pre = p, p += 4 * (size_t)(3 * qkv_rows);
+    p = (p + 15) / 16 * 16;
+    l.pre = p, p += 4 * (size_t)(4 * qkv_rows);
     p = (p + 127) / 128 * 128;
     l.kvs = p, p += 4 * (size_t)(2 * 64 * (head_dim + 16));
+    l.nrm = p, p += 4 * (size_t)embd;
     l.total = (p + 127) / 128 * 128;
     return l;
 }
