@@ -127,6 +127,21 @@ LLMB_API int llmb_get_stats(const llmb_model *m, llmb_stats *out);
 LLMB_API int llmb_generate(llmb_model *m, const int32_t *prompt, int n_prompt, int n, int32_t eos, llmb_emit_fn emit,
                   void *user, int32_t *out_tokens, int *n_out, llmb_timing *tm);
 
+/* Multi-stream generation: n_seq independent greedy sequences on one model
+ * (the reference runs one sequence per GPU object; this is the
+ * llmb_generate_batch of its multi-stream workload).  Sequence s has the
+ * prompt_lens[s] tokens that follow the earlier sequences' in prompts, its
+ * own KV cache (the model keeps an arena of n_seq caches), and Generate's
+ * semantics (gpu.go:946-1014): at most n tokens, eos stops it and is not
+ * emitted.  Each call starts every sequence at position 0.  Prompt tokens
+ * of all sequences go through the layers packed PrefillBatch-style in
+ * batches of 64; then each step decodes one token of every unfinished
+ * sequence, 64 per launch set.  out_tokens receives n_seq rows of n tokens
+ * (row s at s * n), n_out (may be NULL) the count of each row, tm (may be
+ * NULL) the summed timing. */
+LLMB_API int llmb_generate_batch(llmb_model *m, const int32_t *prompts, const int *prompt_lens, int n_seq, int n,
+                                 int32_t eos, int32_t *out_tokens, int *n_out, llmb_timing *tm);
+
 /* PrefillLogits, gpu.go:902-927: runs the prompt and copies the vocab
  * logits of its last token into logits (a test hook: Generate never reads
  * logits back). */

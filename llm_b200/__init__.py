@@ -30,7 +30,8 @@ OK, ERR_ARG, ERR_IO, ERR_FORMAT, ERR_BOUND, ERR_CONFIG, ERR_TENSOR, ERR_MEMORY, 
 
 # Every function include/llm_b200.h declares.
 EXPORTS = ("llmb_open", "llmb_open_reader", "llmb_close", "llmb_last_error", "llmb_get_config", "llmb_memory_used",
-           "llmb_get_stats", "llmb_generate", "llmb_prefill_logits", "llmb_generate_logits", "llmb_peek",
+           "llmb_get_stats", "llmb_generate", "llmb_generate_batch", "llmb_prefill_logits", "llmb_generate_logits",
+           "llmb_peek",
            "llmb_set_layers", "llmb_set_knob", "llmb_get_knob", "llmb_attention_noalloc")
 
 
@@ -80,6 +81,8 @@ def lib() -> C.CDLL:
         L.llmb_get_stats.argtypes, L.llmb_get_stats.restype = [P, C.POINTER(_Stats)], I
         L.llmb_generate.argtypes = [P, P, I, I, C.c_int32, EMIT_FN, P, P, C.POINTER(I), C.POINTER(_Timing)]
         L.llmb_generate.restype = I
+        L.llmb_generate_batch.argtypes = [P, P, P, I, I, C.c_int32, P, P, C.POINTER(_Timing)]
+        L.llmb_generate_batch.restype = I
         L.llmb_prefill_logits.argtypes, L.llmb_prefill_logits.restype = [P, P, I, P], I
         L.llmb_generate_logits.argtypes, L.llmb_generate_logits.restype = [P, P, I, I, P, P], I
         L.llmb_peek.argtypes, L.llmb_peek.restype = [P, C.c_char_p, P, I], I
@@ -226,6 +229,21 @@ class GPU:
                    tm.record_ms, tm.submit_ms, tm.gpu_prefill_ms, tm.gpu_decode_ms, tm.decode_kernel_ms,
                    tm.decode_launches)
         return out[: n_out.value].copy(), t
+
+    def generate_batch(self, prompts, n: int, eos: int = -1) -> tuple[list[np.ndarray], Timing]:
+        """Independent greedy sequences, one KV cache each (llmb_generate_batch): the tokens of each, and the timing."""
+        ps = [np.ascontiguousarray(p, np.int32) for p in prompts]
+        flat = np.concatenate(ps) if ps else np.zeros(0, np.int32)
+        lens = np.array([len(p) for p in ps], np.int32)
+        out = np.zeros((len(ps), max(n, 1)), np.int32)
+        n_out = np.zeros(len(ps), np.int32)
+        tm = _Timing()
+        self._check(lib().llmb_generate_batch(self._h, _ptr(flat), _ptr(lens), len(ps), n, eos, _ptr(out),
+                                              _ptr(n_out), C.byref(tm)))
+        t = Timing(tm.prefill_ms, tm.decode_ms, tm.prompt_tokens, tm.generated, tm.submits, tm.dispatches,
+                   tm.record_ms, tm.submit_ms, tm.gpu_prefill_ms, tm.gpu_decode_ms, tm.decode_kernel_ms,
+                   tm.decode_launches)
+        return [out[i, : n_out[i]].copy() for i in range(len(ps))], t
 
     def prefill_logits(self, prompt) -> np.ndarray:
         """The logits of the prompt's last token (PrefillLogits, gpu.go:904)."""

@@ -50,6 +50,22 @@ struct Layer {
 };
 
 // What the kernels need besides the per-layer descriptors.
+// A batch of up to kMaxPrefill tokens from any sequences (multi-stream
+// decode, and prompt tokens of several sequences): token t (residual row t
+// of x) sits at position pos[t] of the sequence whose KV cache is slot[t] of
+// the arena (slot s, layer l at kv + (s * layers + l) * 2 * ctx * kvd, K
+// then V as in Layer::kv).  The batch head writes the argmax of row
+// head_rows[j] to out[j].
+struct TokBatch {
+    int pos[kMaxPrefill];
+    int slot[kMaxPrefill];
+    int tok[kMaxPrefill];
+    int head_rows[kMaxPrefill];
+    int out[kMaxPrefill];
+    float *kv;
+    int layers;
+};
+
 // One unit of a CTA's weight stream in the persistent decode kernel: one or
 // two source ranges copied into one ring slot.
 struct FeedUnit {

@@ -63,6 +63,7 @@ struct Model {
     cudaEvent_t lev[4][3] = {};  // per decode launch: start, end, tokens copied
     int lk[2] = {0, 0};          // lev index of each launch in flight
     std::vector<void *> allocs;
+    std::vector<size_t> sizes;
     uint64_t used = 0, budget = 0;
     int pm = kMaxPrefill;  // tokens per prefill chunk
     int layers_run = 0;    // GPU.Layers (0: all)
@@ -70,6 +71,10 @@ struct Model {
     DecConfig dec{};
     std::unique_ptr<DecParams> dp;  // the decode kernel's parameter block (header + layers)
     int32_t *h_tokens = nullptr;  // pinned: prompt upload and sampled-token read-back
+    TokBatch *tb = nullptr;       // multi-stream: the token batch (device) and its pinned staging copy
+    TokBatch *h_tb = nullptr;
+    float *bkv = nullptr;         // multi-stream: the KV arena, bkv_slots sequences
+    int bkv_slots = 0;
     uint32_t *h_state = nullptr;
     int *h_err = nullptr;
     llmb_stats stats{};
@@ -79,6 +84,7 @@ struct Model {
         if (st) cudaStreamSynchronize(st);
         for (void *p : allocs) cudaFree(p);
         if (h_tokens) cudaFreeHost(h_tokens);
+        if (h_tb) cudaFreeHost(h_tb);
         if (h_state) cudaFreeHost(h_state);
         if (h_err) cudaFreeHost(h_err);
         if (ev0) cudaEventDestroy(ev0);
@@ -108,8 +114,21 @@ struct Model {
         }
         cudaMemsetAsync(p, 0, bytes, st);
         allocs.push_back(p);
+        sizes.push_back(bytes);
         used += bytes;
         return static_cast<T *>(p);
+    }
+
+    void release(void *p) {
+        for (size_t i = 0; i < allocs.size(); i++)
+            if (allocs[i] == p) {
+                cudaStreamSynchronize(st);
+                cudaFree(p);
+                used -= sizes[i];
+                allocs.erase(allocs.begin() + i);
+                sizes.erase(sizes.begin() + i);
+                return;
+            }
     }
 };
 
@@ -355,8 +374,8 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     if (!(d.att_cnt = m.alloc<uint32_t>((size_t)pm * c.heads * 4, err))) return err;
     if (!(d.state = m.alloc<uint32_t>(8, err))) return err;
     if (!(d.tokens = m.alloc<int32_t>((size_t)(ctx + 1) * 4, err))) return err;
-    if (!(d.am_part = m.alloc<float2>((size_t)head_parts * 8, err))) return err;
-    if (!(d.am_count = m.alloc<uint32_t>(4, err))) return err;
+    if (!(d.am_part = m.alloc<float2>((size_t)head_parts * kMaxPrefill * 8, err))) return err;
+    if (!(d.am_count = m.alloc<uint32_t>(kMaxPrefill * 4, err))) return err;
     if (!(d.err = m.alloc<int>(4, err))) return err;
     if (!(m.bar = m.alloc<GridBarrier>(sizeof(GridBarrier), err))) return err;
     // the persistent decode kernel: tagged activations and its ring configuration
@@ -614,6 +633,143 @@ Error generate(Model &m, const int32_t *prompt, int np, int n, int32_t eos, llmb
     return {LLMB_OK, ""};
 }
 
+// Multi-stream generation (config 5): nseq independent greedy sequences on
+// one model, each with its own KV slot in an arena.  The prompt tokens of all
+// sequences are packed into batches of up to kMaxPrefill tokens, each
+// sequence's in order (a token's attention reads KV rows written by an
+// earlier launch, or by the QKV launch of its own batch, which runs before
+// the batch's attention launch); the last prompt token of a sequence goes
+// through the batch head.  Then every decode step runs one token of each
+// unfinished sequence, kMaxPrefill per launch set.  Per sequence the
+// semantics are Generate's (gpu.go:946-1014): eos stops it and is not
+// emitted, n tokens at most.
+Error ensure_batch(Model &m, int nseq) {
+    Error err{LLMB_OK, ""};
+    if (!m.tb) {
+        if (!(m.tb = m.alloc<TokBatch>(sizeof(TokBatch), err))) return err;
+        CUDA_TRY(cudaHostAlloc(&m.h_tb, sizeof(TokBatch), cudaHostAllocDefault));
+        std::memset(m.h_tb, 0, sizeof(TokBatch));
+    }
+    if (m.bkv_slots < nseq) {
+        if (m.bkv) m.release(m.bkv), m.bkv = nullptr, m.bkv_slots = 0;
+        const size_t per = (size_t)m.cfg.layers * 2 * m.cfg.ctx * m.hdm.kvd;
+        if (!(m.bkv = m.alloc<float>((size_t)nseq * per * 4, err))) return err;
+        m.bkv_slots = nseq;
+    }
+    m.h_tb->kv = m.bkv;
+    m.h_tb->layers = m.cfg.layers;
+    return err;
+}
+
+// Runs the rows staged in m.h_tb (cnt tokens, nh of them through the head)
+// and returns the head's tokens in m.h_tb->out.
+Error run_batch(Model &m, int cnt, int nh) {
+    CUDA_TRY(cudaMemcpyAsync(m.tb, m.h_tb, sizeof(TokBatch), cudaMemcpyHostToDevice, m.st));
+    for (int l = 0; l < m.cfg.layers; l++) launch_layer(m.dm, m.sh, l, cnt, m.st, m.tb);
+    m.stats.dispatches += 5 * m.cfg.layers;
+    if (nh > 0) {
+        launch_head_batch(m.dm, m.sh, m.tb, nh, m.st);
+        m.stats.dispatches++;
+        CUDA_TRY(cudaMemcpyAsync(m.h_tb->out, m.tb->out, (size_t)nh * 4, cudaMemcpyDeviceToHost, m.st));
+    }
+    CUDA_TRY(cudaGetLastError());
+    m.stats.submits++;
+    CUDA_TRY(cudaStreamSynchronize(m.st));
+    return check_device(m);
+}
+
+Error generate_batch(Model &m, const int32_t *prompts, const int *lens, int nseq, int n, int32_t eos, int32_t *out,
+                     int *n_out, llmb_timing *tm_out) {
+    llmb_timing tm{};
+    if (nseq <= 0 || !prompts || !lens) return {LLMB_ERR_ARG, "llm: no sequences"};
+    if (n < 0) return {LLMB_ERR_ARG, "llm: negative token count"};
+    if (n > 0 && !out) return {LLMB_ERR_ARG, "llm: no output buffer"};
+    if (layers_to_run(m) != m.cfg.layers) return {LLMB_ERR_ARG, "llm: generation needs every layer"};
+    std::vector<int64_t> off(nseq + 1, 0);
+    for (int s = 0; s < nseq; s++) {
+        if ((int64_t)lens[s] + n > m.cfg.ctx)
+            return {LLMB_ERR_CONTEXT, "llm: sequence " + std::to_string(s) + ": prompt of " + std::to_string(lens[s]) +
+                                          " tokens and " + std::to_string(n) + " new tokens exceed the context of " +
+                                          std::to_string(m.cfg.ctx)};
+        Error err = check_prompt(m, prompts + off[s], lens[s]);
+        if (err.code) return err;
+        off[s + 1] = off[s] + lens[s];
+    }
+    if (n_out) std::fill(n_out, n_out + nseq, 0);
+    Error err = ensure_batch(m, nseq);
+    if (err.code) return err;
+    const int64_t s0 = m.stats.submits, d0 = m.stats.dispatches;
+    const double t0 = now_ms();
+    CUDA_TRY(cudaEventRecord(m.ev0, m.st));
+    std::vector<int> gen(nseq, 0), last(nseq, 0);
+    std::vector<char> done(nseq, n == 0);
+    auto take = [&](int s, int tok) {  // a sampled token of sequence s
+        if (done[s]) return;
+        if (tok == eos) {
+            done[s] = 1;
+            return;
+        }
+        out[(size_t)s * n + gen[s]] = tok;
+        last[s] = tok;
+        if (++gen[s] >= n) done[s] = 1;
+        tm.generated++;
+        m.stats.tokens++;
+    };
+    // prompts, packed
+    TokBatch &hb = *m.h_tb;
+    int cnt = 0, nh = 0;
+    std::vector<int> head_seq(kMaxPrefill);
+    for (int s = 0; s < nseq; s++) {
+        for (int i = 0; i < lens[s]; i++) {
+            hb.pos[cnt] = i, hb.slot[cnt] = s, hb.tok[cnt] = prompts[off[s] + i];
+            if (i == lens[s] - 1) hb.head_rows[nh] = cnt, head_seq[nh++] = s;
+            if (++cnt == kMaxPrefill) {
+                if ((err = run_batch(m, cnt, nh)).code) return err;
+                for (int j = 0; j < nh; j++) take(head_seq[j], hb.out[j]);
+                cnt = nh = 0;
+            }
+        }
+        tm.prompt_tokens += lens[s];
+    }
+    if (cnt > 0) {
+        if ((err = run_batch(m, cnt, nh)).code) return err;
+        for (int j = 0; j < nh; j++) take(head_seq[j], hb.out[j]);
+    }
+    CUDA_TRY(cudaEventRecord(m.ev1, m.st));
+    tm.prefill_ms = now_ms() - t0;
+    const double t1 = now_ms();
+    CUDA_TRY(cudaEventRecord(m.ev2, m.st));
+    // decode steps: one token of every unfinished sequence
+    std::vector<int> rows;
+    for (;;) {
+        rows.clear();
+        for (int s = 0; s < nseq; s++)
+            if (!done[s]) rows.push_back(s);
+        if (rows.empty()) break;
+        for (size_t a = 0; a < rows.size(); a += kMaxPrefill) {
+            const int c = (int)std::min<size_t>(kMaxPrefill, rows.size() - a);
+            for (int r = 0; r < c; r++) {
+                const int s = rows[a + r];
+                hb.pos[r] = lens[s] + gen[s] - 1, hb.slot[r] = s, hb.tok[r] = last[s], hb.head_rows[r] = r;
+            }
+            if ((err = run_batch(m, c, c)).code) return err;
+            for (int r = 0; r < c; r++) take(rows[a + r], hb.out[r]);
+        }
+    }
+    CUDA_TRY(cudaEventRecord(m.ev3, m.st));
+    CUDA_TRY(cudaEventSynchronize(m.ev3));
+    tm.decode_ms = now_ms() - t1;
+    float a = 0, b = 0;
+    cudaEventElapsedTime(&a, m.ev0, m.ev1);
+    cudaEventElapsedTime(&b, m.ev2, m.ev3);
+    tm.gpu_prefill_ms = a, tm.gpu_decode_ms = b;
+    tm.submits = m.stats.submits - s0, tm.dispatches = m.stats.dispatches - d0;
+    if (n_out)
+        for (int s = 0; s < nseq; s++) n_out[s] = gen[s];
+    if (tm_out) *tm_out = tm;
+    return {LLMB_OK, ""};
+}
+
 Error prefill_logits(Model &m, const int32_t *prompt, int np, float *logits) {
     if (np >= m.cfg.ctx) return {LLMB_ERR_CONTEXT, "llm: prompt longer than the context"};  // gpu.go:905-907
     Error err = check_prompt(m, prompt, np);
@@ -775,6 +931,14 @@ int llmb_generate(llmb_model *mp, const int32_t *prompt, int n_prompt, int n, in
     Model *m = M(mp);
     cudaSetDevice(m->device);
     return fail(m, generate(*m, prompt, n_prompt, n, eos, emit, user, out_tokens, n_out, tm));
+}
+
+int llmb_generate_batch(llmb_model *mp, const int32_t *prompts, const int *prompt_lens, int n_seq, int n, int32_t eos,
+                        int32_t *out_tokens, int *n_out, llmb_timing *tm) {
+    if (!mp) return LLMB_ERR_ARG;
+    Model *m = M(mp);
+    cudaSetDevice(m->device);
+    return fail(m, generate_batch(*m, prompts, prompt_lens, n_seq, n, eos, out_tokens, n_out, tm));
 }
 
 int llmb_prefill_logits(llmb_model *mp, const int32_t *prompt, int n_prompt, float *logits) {

@@ -224,12 +224,18 @@ struct Smem {
 
 __device__ __forceinline__ bool cta_has_tiles(int cta, int ntiles) { return cta < ntiles; }
 
+// Layer l's KV cache for token t: the model's own, or its slot of a batch's arena.
+__device__ __forceinline__ float *kv_of(const DevModel &dm, const TokBatch *tb, int l, int t) {
+    if (!tb) return dm.layer[l].kv;
+    return tb->kv + ((size_t)tb->slot[t] * tb->layers + l) * 2 * (size_t)dm.ctx * dm.kvd;
+}
+
 // K1: RMSNorm + [Wq; Wk; Wv] + bias + RoPE + KV append for token t at
 // position pos (kernels_fused.go:47-73,212-224; cpu.go:279-303).  With
 // from_embed the residual is first taken from the embedding row of tok, and
 // CTA 0 writes it to x.
-__device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bool from_embed, int cta, int ncta,
-                          const Smem &sm) {
+__device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bool from_embed, float *kv, int cta,
+                          int ncta, const Smem &sm) {
     const Layer &L = dm.layer[l];
     const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, nv = L.v.rows >> 3, total = nq + nk + nv;
     if (!cta_has_tiles(cta, total)) return;
@@ -267,8 +273,8 @@ __device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bo
         }
         if ((lane & 3) == 0) {
             if (seg == 0) dm.q[(size_t)t * E + row] = a;
-            else if (seg == 1) L.kv[(size_t)pos * dm.kvd + row] = a;
-            else L.kv[((size_t)dm.ctx + pos) * dm.kvd + row] = a;
+            else if (seg == 1) kv[(size_t)pos * dm.kvd + row] = a;
+            else kv[((size_t)dm.ctx + pos) * dm.kvd + row] = a;
         }
     }
 }
@@ -277,12 +283,12 @@ __device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bo
 // = (head, chunk of kAttnChunk positions): scores, chunk max and exp-sum,
 // exp-weighted V sum (kernels_fused.go:82-146).  The last CTA of a head to
 // finish merges the head's chunks (kernels_fused.go:150-170) into att.
-__device__ void phase_attn(const DevModel &dm, int l, int t, int n, int item, uint32_t *att_cnt, const Smem &sm) {
+__device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, int item, uint32_t *att_cnt,
+                           const Smem &sm) {
     const int HD = dm.head_dim, grp = dm.heads / dm.kv_heads;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
     const int h = item / nch, c = item % nch;
     const int kvh = h / grp;
-    const Layer &L = dm.layer[l];
     float *qh = sm.vec;              // HD
     float *e = sm.vec + HD;          // kAttnChunk
     float *part = sm.vec + HD + kAttnChunk;  // kThreads * 4 doubles (partial V sums)
@@ -296,7 +302,7 @@ __device__ void phase_attn(const DevModel &dm, int l, int t, int n, int item, ui
     {
         double part_s = 0.0;
         if (p < cnt) {
-            const float *kr = L.kv + (size_t)(p0 + p) * dm.kvd + kvh * HD;
+            const float *kr = kv + (size_t)(p0 + p) * dm.kvd + kvh * HD;
             for (int d = sub * 4; d < HD; d += 16) {
                 const float4 k4 = __ldcg(reinterpret_cast<const float4 *>(kr + d));
                 part_s = fma((double)qh[d], (double)k4.x, part_s);
@@ -318,7 +324,7 @@ __device__ void phase_attn(const DevModel &dm, int l, int t, int n, int item, ui
     double o0 = 0, o1 = 0, o2 = 0, o3 = 0;
     for (int pp = g; pp < cnt; pp += G) {
         const double w = e[pp];
-        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(L.kv + ((size_t)dm.ctx + p0 + pp) * dm.kvd + kvh * HD) + d4);
+        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(kv + ((size_t)dm.ctx + p0 + pp) * dm.kvd + kvh * HD) + d4);
         o0 = fma(w, (double)v4.x, o0);
         o1 = fma(w, (double)v4.y, o1);
         o2 = fma(w, (double)v4.z, o2);
@@ -423,7 +429,8 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { retur
 
 // The head: RMSNorm(output_norm) of token t's residual, logits = Wout h
 // (cpu.go:357-363), and this CTA's argmax partial (value, index).
-__device__ void phase_head(const DevModel &dm, int t, int cta, int ncta, const Smem &sm) {
+__device__ void phase_head(const DevModel &dm, int t, int cta, int ncta, float *logits, float2 *am_part,
+                           const Smem &sm) {
     const int E = dm.embd, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int ntiles = dm.head.rows >> 3;
     float *xs = sm.vec + E;
@@ -436,7 +443,7 @@ __device__ void phase_head(const DevModel &dm, int t, int cta, int ncta, const S
         const float a = tile_dot(dm.head, tile, sm.vec, lane);
         const int row = tile * 8 + (lane >> 2);
         if (row < dm.vocab) {
-            if ((lane & 3) == 0) dm.logits[row] = a;
+            if (logits && (lane & 3) == 0) logits[row] = a;
             if (better(a, row, bv, bi)) bv = a, bi = row;
         }
     }
@@ -453,17 +460,17 @@ __device__ void phase_head(const DevModel &dm, int t, int cta, int ncta, const S
     if (threadIdx.x == 0) {
         for (int w = 1; w < kWarps; ++w)
             if (better(wv[w], wi[w], bv, bi)) bv = wv[w], bi = wi[w];
-        dm.am_part[cta] = make_float2(bv, __int_as_float(bi));
+        am_part[cta] = make_float2(bv, __int_as_float(bi));
     }
 }
 
 // The argmax over the CTAs' partials (first index of the largest value).
-__device__ __forceinline__ int reduce_argmax(const DevModel &dm, int nparts, float *red) {
+__device__ __forceinline__ int reduce_argmax(const float2 *am_part, int nparts) {
     __shared__ int result;
     float bv = -FLT_MAX;
     int bi = 0x7fffffff;
     for (int i = threadIdx.x; i < nparts; i += kThreads) {
-        const float2 p = __ldcg(dm.am_part + i);
+        const float2 p = __ldcg(am_part + i);
         const int pi = __float_as_int(p.y);
         if (better(p.x, pi, bv, bi)) bv = p.x, bi = pi;
     }
@@ -492,29 +499,30 @@ __device__ __forceinline__ Smem smem_views(float *base, const DevModel &dm) { re
 
 // ---------------------------------------------------- per-phase kernels --
 
-__global__ void __launch_bounds__(kThreads) k_embed(const DevModel *__restrict__ dmp) {
+__global__ void __launch_bounds__(kThreads) k_embed(const DevModel *__restrict__ dmp, const TokBatch *tb) {
     const DevModel &dm = *dmp;
     const int t = blockIdx.x;
-    const int tok = dm.tokens[dm.state[1] + t];
+    const int tok = tb ? tb->tok[t] : dm.tokens[dm.state[1] + t];
     for (int e = threadIdx.x; e < dm.embd; e += kThreads) dm.x[(size_t)t * dm.embd + e] = gather(dm.embed, tok, e);
 }
 
-__global__ void __launch_bounds__(kThreads) k_qkv(const DevModel *__restrict__ dmp, int l) {
+__global__ void __launch_bounds__(kThreads) k_qkv(const DevModel *__restrict__ dmp, int l, const TokBatch *tb) {
     extern __shared__ float smem[];
     const DevModel &dm = *dmp;
     const int t = blockIdx.y;
-    const int pos = dm.state[0] + t, tok = l == 0 ? dm.tokens[dm.state[1] + t] : 0;
-    phase_qkv(dm, l, t, pos, tok, l == 0, blockIdx.x, gridDim.x, smem_views(smem, dm));
+    const int pos = tb ? tb->pos[t] : dm.state[0] + t;
+    const int tok = l == 0 ? (tb ? tb->tok[t] : dm.tokens[dm.state[1] + t]) : 0;
+    phase_qkv(dm, l, t, pos, tok, l == 0, kv_of(dm, tb, l, t), blockIdx.x, gridDim.x, smem_views(smem, dm));
 }
 
-__global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ dmp, int l) {
+__global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ dmp, int l, const TokBatch *tb) {
     extern __shared__ float smem[];
     const DevModel &dm = *dmp;
     const int t = blockIdx.y;
-    const int n = dm.state[0] + t + 1;
+    const int n = (tb ? tb->pos[t] : dm.state[0] + t) + 1;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
     if ((int)blockIdx.x >= dm.heads * nch) return;
-    phase_attn(dm, l, t, n, blockIdx.x, dm.att_cnt, smem_views(smem, dm));
+    phase_attn(dm, kv_of(dm, tb, l, t), t, n, blockIdx.x, dm.att_cnt, smem_views(smem, dm));
 }
 
 __global__ void __launch_bounds__(kThreads) k_oproj(const DevModel *__restrict__ dmp, int l) {
@@ -538,7 +546,7 @@ __global__ void __launch_bounds__(kThreads) k_head(const DevModel *__restrict__ 
     extern __shared__ float smem[];
     const DevModel &dm = *dmp;
     Smem sm = smem_views(smem, dm);
-    phase_head(dm, t_src, blockIdx.x, gridDim.x, sm);
+    phase_head(dm, t_src, blockIdx.x, gridDim.x, dm.logits, dm.am_part, sm);
     __shared__ int last;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -548,13 +556,38 @@ __global__ void __launch_bounds__(kThreads) k_head(const DevModel *__restrict__ 
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const int tok = reduce_argmax(dm, gridDim.x, sm.red);
+    const int tok = reduce_argmax(dm.am_part, gridDim.x);
     if (threadIdx.x == 0) {
         *dm.am_count = 0;
         const uint32_t step = dm.state[1] + adv;
         dm.tokens[step] = tok;
         dm.state[0] += adv;
         dm.state[1] = step;
+    }
+}
+
+// The batch head: for row j = blockIdx.y, the argmax of token head_rows[j]
+// into out[j] (per-row partials and arrival counters; no logits are kept).
+__global__ void __launch_bounds__(kThreads) k_head_batch(const DevModel *__restrict__ dmp, TokBatch *tb) {
+    extern __shared__ float smem[];
+    const DevModel &dm = *dmp;
+    Smem sm = smem_views(smem, dm);
+    const int j = blockIdx.y;
+    float2 *part = dm.am_part + (size_t)j * gridDim.x;
+    phase_head(dm, tb->head_rows[j], blockIdx.x, gridDim.x, nullptr, part, sm);
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(dm.am_count + j, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int tok = reduce_argmax(part, gridDim.x);
+    if (threadIdx.x == 0) {
+        dm.am_count[j] = 0;
+        tb->out[j] = tok;
     }
 }
 
@@ -609,16 +642,16 @@ void launch_repack(const uint8_t *raw, int rows, int nb, int type, uint8_t *tile
     k_repack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(raw, rows, nb, type, tiles, tile_bytes, dst_row0, neox_hd);
 }
 
-void launch_embed(const DevModel *dm, const Shapes &s, int m, cudaStream_t st) {
-    k_embed<<<m, kThreads, 0, st>>>(dm);
+void launch_embed(const DevModel *dm, const Shapes &s, int m, cudaStream_t st, const TokBatch *tb) {
+    k_embed<<<m, kThreads, 0, st>>>(dm, tb);
 }
 
 static inline unsigned ctas_for(int tiles) { return (unsigned)((tiles + kWarps - 1) / kWarps); }
 
-void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st) {
+void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb) {
     const size_t sh = smem_bytes(s);
-    k_qkv<<<dim3(ctas_for(s.qkv_tiles), m), kThreads, sh, st>>>(dm, l);
-    k_attn<<<dim3(s.heads * s.nchunk, m), kThreads, sh, st>>>(dm, l);
+    k_qkv<<<dim3(ctas_for(s.qkv_tiles), m), kThreads, sh, st>>>(dm, l, tb);
+    k_attn<<<dim3(s.heads * s.nchunk, m), kThreads, sh, st>>>(dm, l, tb);
     k_oproj<<<dim3(ctas_for(s.o_tiles), m), kThreads, sh, st>>>(dm, l);
     k_gateup<<<dim3(ctas_for(s.gu_tiles), m), kThreads, sh, st>>>(dm, l);
     k_down<<<dim3(ctas_for(s.down_tiles), m), kThreads, sh, st>>>(dm, l);
@@ -626,6 +659,10 @@ void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_
 
 void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaStream_t st) {
     k_head<<<s.head_ctas, kThreads, smem_bytes(s), st>>>(dm, t_src, adv);
+}
+
+void launch_head_batch(const DevModel *dm, const Shapes &s, TokBatch *tb, int rows, cudaStream_t st) {
+    k_head_batch<<<dim3(s.head_ctas, rows), kThreads, smem_bytes(s), st>>>(dm, tb);
 }
 
 void launch_advance(const DevModel *dm, int n, cudaStream_t st) { k_advance<<<1, 1, 0, st>>>(dm, n); }

@@ -44,16 +44,21 @@ void launch_repack(const uint8_t *raw, int rows, int nb, int type, uint8_t *tile
 
 // The embedding rows of m tokens into x (the layer-0 kernels fold this in;
 // used alone when no layer runs).
-void launch_embed(const DevModel *dm, const Shapes &s, int m, cudaStream_t st);
+void launch_embed(const DevModel *dm, const Shapes &s, int m, cudaStream_t st, const TokBatch *tb = nullptr);
 
-// One layer for m tokens at positions state.pos .. state.pos+m-1 (5 kernels:
-// norm+QKV+bias+RoPE+KV append, attention partials and merge, output
-// projection + residual, norm+gate/up+SwiGLU, down + residual).
-void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st);
+// One layer for m tokens at positions state.pos .. state.pos+m-1 of the
+// model's sequence, or, with a TokBatch (device memory), token t at position
+// tb->pos[t] of KV slot tb->slot[t] (5 kernels: norm+QKV+bias+RoPE+KV append,
+// attention partials and merge, output projection + residual,
+// norm+gate/up+SwiGLU, down + residual).
+void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb = nullptr);
 
 // Final norm of token t_src's residual, the vocab logits, and the argmax:
 // writes tokens[state.step + adv] and advances state by adv.
 void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaStream_t st);
+
+// The argmax of the residual rows tb->head_rows[0..rows) into tb->out.
+void launch_head_batch(const DevModel *dm, const Shapes &s, TokBatch *tb, int rows, cudaStream_t st);
 
 // state += n.
 void launch_advance(const DevModel *dm, int n, cudaStream_t st);
