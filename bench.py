@@ -222,6 +222,52 @@ def run_reference(args, ws, rank):
     }), flush=True)
 
 
+C5 = synth.WORKLOADS[5]
+
+
+def c5_prompts(vocab, rank):
+    """Config 5's prompts for one GPU: lengths uniform on the range, uniform ids (seeded per rank)."""
+    import numpy as np
+
+    rng = np.random.default_rng(5000 + rank)
+    lo, hi = C5["prompt_range"]
+    lens = rng.integers(lo, hi + 1, C5["streams"])
+    return [synth.prompt_ids(vocab, int(n), seed=10000 * (rank + 1) + i) for i, n in enumerate(lens)]
+
+
+def run_multi_stream(args, ws, rank, local):
+    """Config 5: 64 independent sequences per GPU through llmb_generate_batch; box-total decode tok/s."""
+    import torch
+
+    import llm_b200
+
+    g = llm_b200.GPU(synth.ensure(C5["spec"]), ctx=C5["ctx"], device=local)
+    prompts = c5_prompts(g.cfg.vocab, rank)
+    g.generate_batch(prompts, C5["gen"])  # warm-up (allocates the KV arena)
+    torch.cuda.synchronize()
+    barrier(ws)
+    rounds = max(1, args.c5_rounds)
+    dec = pre = 0.0
+    gen = ptoks = launches = 0
+    for _ in range(rounds):
+        outs, tm = g.generate_batch(prompts, C5["gen"])
+        dec += tm.gpu_decode_ms
+        pre += tm.gpu_prefill_ms
+        gen += tm.generated - len(prompts)  # the first token of each sequence is sampled by the prefill
+        ptoks += tm.prompt_tokens
+        launches += tm.dispatches
+    torch.cuda.synchronize()
+    barrier(ws)
+    g.close()
+    mdec, mpre = all_max([dec, pre], ws)
+    tgen, tpro, tl = all_sum([gen, ptoks, launches], ws)
+    return {"workload": f"config 5: {C5['streams']} sequences per GPU on {C5['spec'].name}, prompts uniform on "
+                        f"{list(C5['prompt_range'])}, {C5['gen']} greedy tokens each, ctx {C5['ctx']}",
+            "decode_tok_s": tgen / (mdec / 1000.0), "prefill_tok_s": tpro / (mpre / 1000.0), "unit": "tok/s",
+            "rounds": rounds, "decode_ms_per_round": mdec / rounds, "prefill_ms_per_round": mpre / rounds,
+            "gpu_launches": int(tl), "timing": "CUDA events on the library stream, max over ranks; box total"}
+
+
 def run_ours(args, ws, rank, local):
     import torch
 
@@ -256,6 +302,7 @@ def run_ours(args, ws, rank, local):
                   all_max([acc["dec"], acc["pre"], acc["kern"], acc["wall_dec"], acc["wall_pre"]], ws)))
     launches_total, dispatches_total = all_sum([acc["launches"], acc["dispatches"]], ws)
     g.close()
+    multi = None if args.no_multi_stream else run_multi_stream(args, ws, rank, local)
     if rank != 0:
         return
     K = args.steps
@@ -291,6 +338,8 @@ def run_ours(args, ws, rank, local):
     }
     if cpu:
         out["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if multi:
+        out["multi_stream"] = multi
     print(json.dumps(out), flush=True)
 
 
@@ -301,6 +350,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-multi-stream", action="store_true", help="skip the config 5 (64-sequence) measurement")
+    ap.add_argument("--c5-rounds", type=int, default=1, help="timed rounds of config 5")
     args = ap.parse_args()
     ws, rank, local = dist_setup()
     try:
