@@ -15,7 +15,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libllmb200.so")
-SOURCES = ["gguf.cpp", "kernels.cu", "decode.cu", "engine.cu", "noalloc.cu"]
+SOURCES = ["gguf.cpp", "kernels.cu", "gemm.cu", "decode.cu", "engine.cu", "noalloc.cu"]
 HEADERS = ["gguf.hpp", "device.hpp", "kernels.hpp", os.path.join("..", "..", "include", "llm_b200.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", os.path.join(ROOT, "include")]

@@ -99,6 +99,10 @@ struct ModelHeader {
     float2 *am_part;   // argmax partials per CTA (value, index as float bits)
     uint32_t *am_count;// arrival counter of the head kernel's CTAs
     int *err;          // device error word (0 = none)
+    // the m-token products (gemm.cu): normed rows [kMaxPrefill][embd], the
+    // head's per (token, row tile) argmax partials
+    float *h;
+    float2 *gam;
 
     // the persistent decode kernel's tagged activations ({f32 value, u32 tag})
     uint64_t *ll_x, *ll_q, *ll_k, *ll_v, *ll_att, *ll_act, *ll_pv, *ll_ml;

@@ -18,6 +18,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <map>
 #include <vector>
 
 #include "../../include/llm_b200.h"
@@ -33,7 +34,8 @@ std::atomic<int64_t> g_decode_batch{8};
 std::atomic<int64_t> g_prefill_batch{kMaxPrefill};
 std::atomic<int64_t> g_memory_budget{0};
 std::atomic<int64_t> g_decode_mode{0};  // 0: persistent kernel, 1: per-phase kernels
-std::atomic<int64_t> g_decode_trace{0}; // 1: record the persistent kernel's phase timeline (read by llmb_peek "trace")
+std::atomic<int64_t> g_decode_trace{0};
+std::atomic<int64_t> g_prefill_mode{0};  // 0: chunked products (gemm.cu), 1: the per-token kernels // 1: record the persistent kernel's phase timeline (read by llmb_peek "trace")
 
 thread_local std::string t_open_error;
 
@@ -75,6 +77,9 @@ struct Model {
     TokBatch *h_tb = nullptr;
     float *bkv = nullptr;         // multi-stream: the KV arena, bkv_slots sequences
     int bkv_slots = 0;
+    // the m-token layer sequences (embedding + every layer's launches), captured once per
+    // (tokens, batch or single sequence, layers) and replayed: a step of 64 sequences is ~210 launches
+    std::map<int64_t, cudaGraphExec_t> graphs;
     uint32_t *h_state = nullptr;
     int *h_err = nullptr;
     llmb_stats stats{};
@@ -85,6 +90,7 @@ struct Model {
         for (void *p : allocs) cudaFree(p);
         if (h_tokens) cudaFreeHost(h_tokens);
         if (h_tb) cudaFreeHost(h_tb);
+        for (auto &g : graphs) cudaGraphExecDestroy(g.second);
         if (h_state) cudaFreeHost(h_state);
         if (h_err) cudaFreeHost(h_err);
         if (ev0) cudaEventDestroy(ev0);
@@ -307,6 +313,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, m.device));
     s.head_ctas = std::max(1, std::min(nsm * 2, (s.head_tiles + kWarps - 1) / kWarps));
     d.smem_vec = smem_vec_floats(s);
+    CUDA_TRY(prepare_kernels(s));
     m.persistent_ctas = nsm;
 
     Error err{LLMB_OK, ""};
@@ -375,6 +382,8 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     if (!(d.state = m.alloc<uint32_t>(8, err))) return err;
     if (!(d.tokens = m.alloc<int32_t>((size_t)(ctx + 1) * 4, err))) return err;
     if (!(d.am_part = m.alloc<float2>((size_t)head_parts * kMaxPrefill * 8, err))) return err;
+    if (!(d.h = m.alloc<float>((size_t)pm * E * 4, err))) return err;
+    if (!(d.gam = m.alloc<float2>((size_t)pm * ((d.head.rows + 63) / 64) * 8, err))) return err;
     if (!(d.am_count = m.alloc<uint32_t>(kMaxPrefill * 4, err))) return err;
     if (!(d.err = m.alloc<int>(4, err))) return err;
     if (!(m.bar = m.alloc<GridBarrier>(sizeof(GridBarrier), err))) return err;
@@ -479,6 +488,31 @@ Error begin(Model &m, const int32_t *prompt, int n) {
     return {LLMB_OK, ""};
 }
 
+// The embedding and nl layers of cnt tokens through the chunked products,
+// as a CUDA graph captured on first use (the kernels read positions, tokens
+// and KV slots from device memory, so one graph serves every call).
+Error run_layers_mm(Model &m, int cnt, int nl, const TokBatch *tb) {
+    const int64_t key = ((int64_t)cnt * 2 + (tb ? 1 : 0)) * 1024 + nl;
+    auto it = m.graphs.find(key);
+    if (it == m.graphs.end()) {
+        CUDA_TRY(cudaStreamBeginCapture(m.st, cudaStreamCaptureModeThreadLocal));
+        launch_embed(m.dm, m.sh, cnt, m.st, tb);
+        cudaError_t e = cudaGetLastError();
+        for (int l = 0; l < nl && e == cudaSuccess; l++)
+            e = launch_layer_mm(m.dm, m.hdm, m.sh, l, cnt, m.persistent_ctas, m.st, tb);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e2 = cudaStreamEndCapture(m.st, &g);
+        if (e == cudaSuccess) e = e2;
+        cudaGraphExec_t ex = nullptr;
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+        if (g) cudaGraphDestroy(g);
+        CUDA_TRY(e);
+        it = m.graphs.emplace(key, ex).first;
+    }
+    CUDA_TRY(cudaGraphLaunch(it->second, m.st));
+    return {LLMB_OK, ""};
+}
+
 // prefill (gpu.go:853-900) over chunks of pm tokens (chunk, fused.go:294-320):
 // the last chunk's last token goes through the head, which samples tokens[n].
 Error prefill(Model &m, int n) {
@@ -487,12 +521,18 @@ Error prefill(Model &m, int n) {
     for (int a = 0; a < n; a += m.pm) {
         const int cnt = std::min(m.pm, n - a);
         const bool last = a + cnt == n;
-        if (nl == 0) {
-            launch_embed(m.dm, m.sh, cnt, m.st);
-            m.stats.dispatches++;
+        if (g_prefill_mode.load() == 0) {
+            Error e = run_layers_mm(m, cnt, nl, nullptr);
+            if (e.code) return e;
+            m.stats.dispatches += 1 + 7 * nl;
+        } else {
+            if (nl == 0) {
+                launch_embed(m.dm, m.sh, cnt, m.st);
+                m.stats.dispatches++;
+            }
+            for (int l = 0; l < nl; l++) launch_layer(m.dm, m.sh, l, cnt, m.st);
+            m.stats.dispatches += 5 * nl;
         }
-        for (int l = 0; l < nl; l++) launch_layer(m.dm, m.sh, l, cnt, m.st);
-        m.stats.dispatches += 5 * nl;
         if (last && head) launch_head(m.dm, m.sh, cnt - 1, cnt, m.st);
         else launch_advance(m.dm, cnt, m.st);
         m.stats.dispatches++;
@@ -665,11 +705,19 @@ Error ensure_batch(Model &m, int nseq) {
 // and returns the head's tokens in m.h_tb->out.
 Error run_batch(Model &m, int cnt, int nh) {
     CUDA_TRY(cudaMemcpyAsync(m.tb, m.h_tb, sizeof(TokBatch), cudaMemcpyHostToDevice, m.st));
-    for (int l = 0; l < m.cfg.layers; l++) launch_layer(m.dm, m.sh, l, cnt, m.st, m.tb);
-    m.stats.dispatches += 5 * m.cfg.layers;
+    const bool mm = g_prefill_mode.load() == 0;
+    if (mm) {
+        Error e = run_layers_mm(m, cnt, m.cfg.layers, m.tb);
+        if (e.code) return e;
+        m.stats.dispatches += 1 + 7 * m.cfg.layers;
+    } else {
+        for (int l = 0; l < m.cfg.layers; l++) launch_layer(m.dm, m.sh, l, cnt, m.st, m.tb);
+        m.stats.dispatches += 5 * m.cfg.layers;
+    }
     if (nh > 0) {
-        launch_head_batch(m.dm, m.sh, m.tb, nh, m.st);
-        m.stats.dispatches++;
+        if (mm) CUDA_TRY(launch_head_mm(m.dm, m.hdm, m.sh, m.tb, m.tb->head_rows, nh, m.persistent_ctas, m.st));
+        else launch_head_batch(m.dm, m.sh, m.tb, nh, m.st);
+        m.stats.dispatches += mm ? 3 : 1;
         CUDA_TRY(cudaMemcpyAsync(m.h_tb->out, m.tb->out, (size_t)nh * 4, cudaMemcpyDeviceToHost, m.st));
     }
     CUDA_TRY(cudaGetLastError());
@@ -977,6 +1025,7 @@ int llmb_set_knob(const char *name, int64_t v) {
     else if (s == "memory_budget") g_memory_budget = std::max<int64_t>(v, 0);
     else if (s == "decode_mode") g_decode_mode = v ? 1 : 0;
     else if (s == "decode_trace") g_decode_trace = v ? 1 : 0;
+    else if (s == "prefill_mode") g_prefill_mode = v ? 1 : 0;
     else return LLMB_ERR_ARG;
     return LLMB_OK;
 }
@@ -989,6 +1038,7 @@ int64_t llmb_get_knob(const char *name) {
     if (s == "memory_budget") return g_memory_budget;
     if (s == "decode_mode") return g_decode_mode;
     if (s == "decode_trace") return g_decode_trace;
+    if (s == "prefill_mode") return g_prefill_mode;
     return -1;
 }
 

@@ -25,8 +25,10 @@
 // persistent decode kernel is in decode.cu.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
+#include <mutex>
 
 #include "kernels.hpp"
 
@@ -280,84 +282,102 @@ __device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bo
 }
 
 // K2 + the merge of K3: attention of token t (n positions visible) for item
-// = (head, chunk of kAttnChunk positions): scores, chunk max and exp-sum,
-// exp-weighted V sum (kernels_fused.go:82-146).  The last CTA of a head to
-// finish merges the head's chunks (kernels_fused.go:150-170) into att.
+// = (KV head g, chunk of kAttnChunk positions), for every query head of g's
+// GQA group (cpu.go:304-335): the chunk's K and V rows are read once into
+// shared memory and serve the group's heads; per head the scores, the chunk
+// max and exp-sum and the exp-weighted V sum (kernels_fused.go:82-146), in
+// double.  The last CTA of (token, group) to finish merges the chunks of the
+// group's heads (kernels_fused.go:150-170) into att.
 __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, int item, uint32_t *att_cnt,
                            const Smem &sm) {
     const int HD = dm.head_dim, grp = dm.heads / dm.kv_heads;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
-    const int h = item / nch, c = item % nch;
-    const int kvh = h / grp;
-    float *qh = sm.vec;              // HD
-    float *e = sm.vec + HD;          // kAttnChunk
-    float *part = sm.vec + HD + kAttnChunk;  // kThreads * 4 doubles (partial V sums)
+    const int g = item / nch, c = item % nch;
+    const int KS = HD + 4;                       // shared row stride
+    float *ks = sm.vec;                          // [kAttnChunk][KS]
+    float *vs = ks + kAttnChunk * KS;            // [kAttnChunk][KS]
+    float *qg = vs + kAttnChunk * KS;            // [grp][HD]
+    float *e = qg + grp * HD;                    // [kAttnChunk]
+    double *dpart = reinterpret_cast<double *>(e + kAttnChunk + 2);  // kThreads * 4 doubles (8-byte aligned)
     __shared__ int last;
-    for (int i = threadIdx.x; i < HD; i += kThreads) qh[i] = __ldcg(dm.q + (size_t)t * dm.embd + h * HD + i);
-    __syncthreads();
     const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
-    // scores: 4 threads per position, HD/4 dims each, accumulated in double
+    const int nd4 = HD / 4;
+    for (int i = threadIdx.x; i < cnt * nd4; i += kThreads) {
+        const int p = i / nd4, d4 = i % nd4;
+        const size_t row = (size_t)(p0 + p) * dm.kvd + g * HD;
+        *reinterpret_cast<float4 *>(ks + p * KS + d4 * 4) = __ldcg(reinterpret_cast<const float4 *>(kv + row) + d4);
+        *reinterpret_cast<float4 *>(vs + p * KS + d4 * 4) =
+            __ldcg(reinterpret_cast<const float4 *>(kv + (size_t)dm.ctx * dm.kvd + row) + d4);
+    }
+    for (int i = threadIdx.x; i < grp * HD; i += kThreads) qg[i] = __ldcg(dm.q + (size_t)t * dm.embd + g * grp * HD + i);
+    __syncthreads();
     const int p = threadIdx.x >> 2, sub = threadIdx.x & 3;
-    float s = -FLT_MAX;
-    {
-        double part_s = 0.0;
-        if (p < cnt) {
-            const float *kr = kv + (size_t)(p0 + p) * dm.kvd + kvh * HD;
-            for (int d = sub * 4; d < HD; d += 16) {
-                const float4 k4 = __ldcg(reinterpret_cast<const float4 *>(kr + d));
-                part_s = fma((double)qh[d], (double)k4.x, part_s);
-                part_s = fma((double)qh[d + 1], (double)k4.y, part_s);
-                part_s = fma((double)qh[d + 2], (double)k4.z, part_s);
-                part_s = fma((double)qh[d + 3], (double)k4.w, part_s);
+    const int G = kThreads / nd4, d4 = threadIdx.x % nd4, gi = threadIdx.x / nd4;
+    for (int j = 0; j < grp; ++j) {
+        const int h = g * grp + j;
+        const float *qh = qg + j * HD;
+        // scores: 4 threads per position, HD/4 dims each, accumulated in double
+        float s = -FLT_MAX;
+        {
+            double part_s = 0.0;
+            if (p < cnt) {
+                const float *kr = ks + p * KS;
+                for (int d = sub * 4; d < HD; d += 16) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+                    part_s = fma((double)qh[d], (double)k4.x, part_s);
+                    part_s = fma((double)qh[d + 1], (double)k4.y, part_s);
+                    part_s = fma((double)qh[d + 2], (double)k4.z, part_s);
+                    part_s = fma((double)qh[d + 3], (double)k4.w, part_s);
+                }
             }
+            part_s += __shfl_xor_sync(kFull, part_s, 1);
+            part_s += __shfl_xor_sync(kFull, part_s, 2);
+            if (p < cnt) s = __fmul_rn((float)part_s, dm.scale);
         }
-        part_s += __shfl_xor_sync(kFull, part_s, 1);
-        part_s += __shfl_xor_sync(kFull, part_s, 2);
-        if (p < cnt) s = __fmul_rn((float)part_s, dm.scale);
+        const float mx = block_max(s, sm.red);
+        if (p < cnt && sub == 0) e[p] = (float)exp((double)__fsub_rn(s, mx));
+        __syncthreads();
+        // V sum: thread (d4, gi): float4 d4 of the head, positions gi, gi + G, ..., in double
+        double o0 = 0, o1 = 0, o2 = 0, o3 = 0;
+        for (int pp = gi; pp < cnt; pp += G) {
+            const double w = e[pp];
+            const float4 v4 = *reinterpret_cast<const float4 *>(vs + pp * KS + d4 * 4);
+            o0 = fma(w, (double)v4.x, o0);
+            o1 = fma(w, (double)v4.y, o1);
+            o2 = fma(w, (double)v4.z, o2);
+            o3 = fma(w, (double)v4.w, o3);
+        }
+        dpart[threadIdx.x * 4 + 0] = o0, dpart[threadIdx.x * 4 + 1] = o1;
+        dpart[threadIdx.x * 4 + 2] = o2, dpart[threadIdx.x * 4 + 3] = o3;
+        __syncthreads();
+        const size_t th = (size_t)t * dm.heads + h;
+        if (threadIdx.x < nd4) {
+            double tot[4] = {0, 0, 0, 0};
+            for (int k = 0; k < G; ++k)
+                for (int q4 = 0; q4 < 4; ++q4) tot[q4] += dpart[(threadIdx.x + k * nd4) * 4 + q4];
+            for (int q4 = 0; q4 < 4; ++q4) dm.part_pv[(th * dm.nchunk + c) * HD + threadIdx.x * 4 + q4] = (float)tot[q4];
+        }
+        if (threadIdx.x == 0) {
+            double lsum = 0.0;
+            for (int pp = 0; pp < cnt; ++pp) lsum += e[pp];
+            dm.part_ml[th * dm.nchunk + c] = make_float2(mx, (float)lsum);
+        }
+        __syncthreads();  // e and dpart are reused by the next head
     }
-    const float mx = block_max(s, sm.red);
-    if (p < cnt && sub == 0) e[p] = (float)exp((double)__fsub_rn(s, mx));
-    __syncthreads();
-    // V sum: thread (d4, g): float4 d4 of the head, positions g, g+G, ..., in double
-    const int nd4 = HD / 4, G = kThreads / nd4;
-    const int d4 = threadIdx.x % nd4, g = threadIdx.x / nd4;
-    double o0 = 0, o1 = 0, o2 = 0, o3 = 0;
-    for (int pp = g; pp < cnt; pp += G) {
-        const double w = e[pp];
-        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(kv + ((size_t)dm.ctx + p0 + pp) * dm.kvd + kvh * HD) + d4);
-        o0 = fma(w, (double)v4.x, o0);
-        o1 = fma(w, (double)v4.y, o1);
-        o2 = fma(w, (double)v4.z, o2);
-        o3 = fma(w, (double)v4.w, o3);
-    }
-    double *dpart = reinterpret_cast<double *>(part);
-    dpart[threadIdx.x * 4 + 0] = o0, dpart[threadIdx.x * 4 + 1] = o1;
-    dpart[threadIdx.x * 4 + 2] = o2, dpart[threadIdx.x * 4 + 3] = o3;
-    __syncthreads();
-    const size_t th = (size_t)t * dm.heads + h;
-    if (threadIdx.x < nd4) {
-        double tot[4] = {0, 0, 0, 0};
-        for (int k = 0; k < G; ++k)
-            for (int j = 0; j < 4; ++j) tot[j] += dpart[(threadIdx.x + k * nd4) * 4 + j];
-        for (int j = 0; j < 4; ++j) dm.part_pv[(th * dm.nchunk + c) * HD + threadIdx.x * 4 + j] = (float)tot[j];
-    }
-    if (threadIdx.x == 0) {
-        double lsum = 0.0;
-        for (int pp = 0; pp < cnt; ++pp) lsum += e[pp];
-        dm.part_ml[th * dm.nchunk + c] = make_float2(mx, (float)lsum);
-    }
-    // the last arriving CTA of this head merges its chunks
-    __syncthreads();
+    // the last arriving CTA of this (token, group) merges the group's heads
+    const size_t tg = (size_t)t * dm.kv_heads + g;
     if (threadIdx.x == 0) {
         __threadfence();
-        const unsigned prev = atomicAdd(att_cnt + th, 1u);
+        const unsigned prev = atomicAdd(att_cnt + tg, 1u);
         last = prev == (unsigned)(nch - 1);
-        if (last) att_cnt[th] = 0;
+        if (last) att_cnt[tg] = 0;
     }
     __syncthreads();
     if (!last) return;
     __threadfence();
-    for (int d = threadIdx.x; d < HD; d += kThreads) {
+    for (int i = threadIdx.x; i < grp * HD; i += kThreads) {
+        const int j = i / HD, d = i % HD, h = g * grp + j;
+        const size_t th = (size_t)t * dm.heads + h;
         float M = -FLT_MAX;
         for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(&dm.part_ml[th * dm.nchunk + cc].x));
         double lt = 0.0, ot = 0.0;
@@ -521,7 +541,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ 
     const int t = blockIdx.y;
     const int n = (tb ? tb->pos[t] : dm.state[0] + t) + 1;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
-    if ((int)blockIdx.x >= dm.heads * nch) return;
+    if ((int)blockIdx.x >= dm.kv_heads * nch) return;
     phase_attn(dm, kv_of(dm, tb, l, t), t, n, blockIdx.x, dm.att_cnt, smem_views(smem, dm));
 }
 
@@ -630,11 +650,29 @@ __global__ void k_repack(const uint8_t *__restrict__ raw, int rows, int nb, int 
 
 int smem_vec_floats(const Shapes &s) {
     const int vec = s.embd + (s.embd > s.ff ? s.embd : s.ff);
-    const int attn = s.head_dim + kAttnChunk + 8 * kThreads;
+    // attention: K and V chunks, the group's queries, exp weights, double partials
+    const int attn = 2 * kAttnChunk * (s.head_dim + 4) + (s.heads / s.kv_heads) * s.head_dim + kAttnChunk + 2 +
+                     8 * kThreads;
     return vec > attn ? vec : attn;
 }
 
 size_t smem_bytes(const Shapes &s) { return ((size_t)smem_vec_floats(s) + 2 * kWarps) * sizeof(float); }
+
+cudaError_t prepare_kernels(const Shapes &s) {
+    // the attribute is per function, for the whole process: only ever raise it, so that
+    // opening a smaller model does not break the kernels of a larger one still open
+    static std::mutex mu;
+    static int set = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    const int sh = std::max(set, (int)smem_bytes(s));
+    if (sh == set) return cudaSuccess;
+    set = sh;
+    cudaError_t e = cudaSuccess;
+    for (const void *k : {(const void *)k_qkv, (const void *)k_attn, (const void *)k_oproj, (const void *)k_gateup,
+                          (const void *)k_down, (const void *)k_head, (const void *)k_head_batch})
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sh);
+    return e;
+}
 
 void launch_repack(const uint8_t *raw, int rows, int nb, int type, uint8_t *tiles, int tile_bytes, int dst_row0,
                    int neox_hd, cudaStream_t st) {
@@ -651,7 +689,7 @@ static inline unsigned ctas_for(int tiles) { return (unsigned)((tiles + kWarps -
 void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb) {
     const size_t sh = smem_bytes(s);
     k_qkv<<<dim3(ctas_for(s.qkv_tiles), m), kThreads, sh, st>>>(dm, l, tb);
-    k_attn<<<dim3(s.heads * s.nchunk, m), kThreads, sh, st>>>(dm, l, tb);
+    k_attn<<<dim3(s.kv_heads * s.nchunk, m), kThreads, sh, st>>>(dm, l, tb);
     k_oproj<<<dim3(ctas_for(s.o_tiles), m), kThreads, sh, st>>>(dm, l);
     k_gateup<<<dim3(ctas_for(s.gu_tiles), m), kThreads, sh, st>>>(dm, l);
     k_down<<<dim3(ctas_for(s.down_tiles), m), kThreads, sh, st>>>(dm, l);
@@ -659,6 +697,10 @@ void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_
 
 void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaStream_t st) {
     k_head<<<s.head_ctas, kThreads, smem_bytes(s), st>>>(dm, t_src, adv);
+}
+
+void launch_attention(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb) {
+    k_attn<<<dim3(s.kv_heads * s.nchunk, m), kThreads, smem_bytes(s), st>>>(dm, l, tb);
 }
 
 void launch_head_batch(const DevModel *dm, const Shapes &s, TokBatch *tb, int rows, cudaStream_t st) {

@@ -34,6 +34,8 @@ constexpr int kThreads = kWarps * 32; // threads per CTA
 // Dynamic shared memory of every kernel: a vector region, then reduction scratch.
 int smem_vec_floats(const Shapes &s);
 size_t smem_bytes(const Shapes &s);
+// Lets the per-phase kernels use smem_bytes(s) of dynamic shared memory.
+cudaError_t prepare_kernels(const Shapes &s);
 
 // Repacks `rows` raw GGUF rows (blocks of `type`) staged in device memory
 // into the tile layout at destination row dst_row0.  neox_hd > 0 reorders the
@@ -56,6 +58,20 @@ void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_
 // Final norm of token t_src's residual, the vocab logits, and the argmax:
 // writes tokens[state.step + adv] and advances state by adv.
 void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaStream_t st);
+
+// The attention of one layer alone (the m-token path's products are in gemm.cu).
+void launch_attention(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb);
+
+// One layer for m <= 64 tokens through the chunked products of gemm.cu
+// (norm, QKV product with bias/RoPE/KV append, attention, output product +
+// residual, norm, gate/up product + SwiGLU, down product + residual); hd is
+// the host copy of *dm (device pointers), nsm the SMs to fill.
+cudaError_t launch_layer_mm(const DevModel *dm, const DevModel &hd, const Shapes &s, int l, int m, int nsm,
+                            cudaStream_t st, const TokBatch *tb);
+// The head for `rows` residual rows listed at rows_dev (device): final norm,
+// the vocabulary product and the argmax of each row into tb->out.
+cudaError_t launch_head_mm(const DevModel *dm, const DevModel &hd, const Shapes &s, TokBatch *tb, const int *rows_dev,
+                           int rows, int nsm, cudaStream_t st);
 
 // The argmax of the residual rows tb->head_rows[0..rows) into tb->out.
 void launch_head_batch(const DevModel *dm, const Shapes &s, TokBatch *tb, int rows, cudaStream_t st);
