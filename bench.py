@@ -243,14 +243,15 @@ def run_multi_stream(args, ws, rank, local):
 
     g = llm_b200.GPU(synth.ensure(C5["spec"]), ctx=C5["ctx"], device=local)
     prompts = c5_prompts(g.cfg.vocab, rank)
-    g.generate_batch(prompts, C5["gen"])  # warm-up (allocates the KV arena)
+    ngen = args.c5_gen or C5["gen"]
+    g.generate_batch(prompts, ngen)  # warm-up (allocates the KV arena)
     torch.cuda.synchronize()
     barrier(ws)
     rounds = max(1, args.c5_rounds)
     dec = pre = 0.0
     gen = ptoks = launches = 0
     for _ in range(rounds):
-        outs, tm = g.generate_batch(prompts, C5["gen"])
+        outs, tm = g.generate_batch(prompts, ngen)
         dec += tm.gpu_decode_ms
         pre += tm.gpu_prefill_ms
         gen += tm.generated - len(prompts)  # the first token of each sequence is sampled by the prefill
@@ -262,7 +263,7 @@ def run_multi_stream(args, ws, rank, local):
     mdec, mpre = all_max([dec, pre], ws)
     tgen, tpro, tl = all_sum([gen, ptoks, launches], ws)
     return {"workload": f"config 5: {C5['streams']} sequences per GPU on {C5['spec'].name}, prompts uniform on "
-                        f"{list(C5['prompt_range'])}, {C5['gen']} greedy tokens each, ctx {C5['ctx']}",
+                        f"{list(C5['prompt_range'])}, {ngen} greedy tokens each, ctx {C5['ctx']}",
             "decode_tok_s": tgen / (mdec / 1000.0), "prefill_tok_s": tpro / (mpre / 1000.0), "unit": "tok/s",
             "rounds": rounds, "decode_ms_per_round": mdec / rounds, "prefill_ms_per_round": mpre / rounds,
             "gpu_launches": int(tl), "timing": "CUDA events on the library stream, max over ranks; box total"}
@@ -352,11 +353,21 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-multi-stream", action="store_true", help="skip the config 5 (64-sequence) measurement")
     ap.add_argument("--c5-rounds", type=int, default=1, help="timed rounds of config 5")
+    ap.add_argument("--c5-gen", type=int, default=0, help="greedy tokens per config 5 sequence (0: the workload's 128)")
+    ap.add_argument("--only-multi-stream", action="store_true",
+                    help="run only the config 5 measurement and print its object (a profiling aid)")
     args = ap.parse_args()
     ws, rank, local = dist_setup()
     try:
         if args.impl == "reference":
             run_reference(args, ws, rank)
+        elif args.only_multi_stream:
+            import torch
+
+            torch.cuda.set_device(local)
+            multi = run_multi_stream(args, ws, rank, local)
+            if rank == 0:
+                print(json.dumps({"multi_stream": multi}), flush=True)
         else:
             run_ours(args, ws, rank, local)
     finally:

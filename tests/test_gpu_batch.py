@@ -64,6 +64,21 @@ def test_batch_more_sequences_than_a_launch(oracle, gpus):
         assert np.array_equal(got[i], cpu.generate(p, n)), i
 
 
+def test_batch_per_token_kernels(oracle, gpus):
+    """prefill_mode 1: the same batches through the per-token kernels."""
+    g = gpus("tiny-mixed", 256)
+    prompts = prompts_for(g.cfg.vocab, [3, 66, 20], seed=80)
+    old = llm_b200.get_knob("prefill_mode")
+    llm_b200.set_knob("prefill_mode", 1)
+    try:
+        got, _ = g.generate_batch(prompts, 12)
+    finally:
+        llm_b200.set_knob("prefill_mode", old)
+    cpu = oracle.CPU(synth.ensure("tiny-mixed"), 256)
+    for i, p in enumerate(prompts):
+        assert np.array_equal(got[i], cpu.generate(p, 12)), i
+
+
 def test_batch_benchmark_model(oracle, gpus):
     g = gpus("c1-smollm2-q4_0", 512)
     lens = [16, 40, 9]

@@ -93,6 +93,26 @@ def test_prefill_logits(oracle, gpus, spec, n_prompt):
     assert int(np.argmax(got)) == oracle.argmax(want)
 
 
+@pytest.mark.parametrize("spec", ["tiny-llama", "tiny-mixed", "tiny-qwen2", "c3-qwen2.5-0.5b"])
+def test_prefill_per_token_kernels(oracle, gpus, spec):
+    """prefill_mode 1 (one matvec per token and phase) against the oracle, and against the products' path."""
+    old = llm_b200.get_knob("prefill_mode")
+    g = gpus(spec, 256)
+    prompt = synth.prompt_ids(g.cfg.vocab, 70, seed=21)
+    try:
+        llm_b200.set_knob("prefill_mode", 1)
+        got1 = g.prefill_logits(prompt)
+    finally:
+        llm_b200.set_knob("prefill_mode", old)
+    got0 = g.prefill_logits(prompt)
+    cpu = oracle.CPU(synth.ensure(spec), 256)
+    for t in prompt:
+        want = cpu.forward(int(t))
+    for got in (got0, got1):
+        assert rel_err(got, want) <= REL_TOL
+        assert int(np.argmax(got)) == oracle.argmax(want)
+
+
 @pytest.mark.parametrize("spec", ["tiny-llama", "tiny-mixed", "tiny-qwen2"])
 def test_generate_every_step(oracle, gpus, decode_mode, spec):
     """Every decoded step's logits and token against the oracle's greedy run."""
