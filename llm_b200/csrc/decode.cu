@@ -4,8 +4,8 @@
 //
 // Structure of a CTA (one per SM, 8 warps, so up to 255 registers a thread):
 //   - the CTA's weight tiles stream, in the order the CTA consumes them,
-//     through a ring of shared-memory slots with 1D bulk TMA copies
-//     (cp.async.bulk, no multicast) tracked by mbarriers.  One thread issues
+//     through a ring of shared-memory slots with 1D bulk TMA copies into
+//     this CTA's own shared memory, tracked by mbarriers.  One thread issues
 //     them and refills each slot as soon as its unit is consumed.  Weights do
 //     not depend on activations, so the stream runs ahead across phases,
 //     layers and tokens as far as the ring allows;
