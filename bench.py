@@ -269,6 +269,25 @@ def run_multi_stream(args, ws, rank, local):
             "gpu_launches": int(tl), "timing": "CUDA events on the library stream, max over ranks; box total"}
 
 
+def run_other_configs(local):
+    """Configs 2-4 once each (after a warm-up run): decode and prefill tok/s by CUDA events, one GPU."""
+    import llm_b200
+
+    out = {}
+    for k in (2, 3, 4):
+        w = synth.WORKLOADS[k]
+        g = llm_b200.GPU(synth.ensure(w["spec"]), ctx=w["ctx"], device=local)
+        prompt = synth.prompt_ids(g.cfg.vocab, w["prompt"], seed=w["spec"].seed)
+        g.generate(prompt, w["gen"])
+        _, tm = g.generate(prompt, w["gen"])
+        g.close()
+        out[f"config{k}"] = {"workload": f"{w['spec'].name}: {w['prompt']}-token prompt + {w['gen']} greedy tokens, "
+                                         f"ctx {w['ctx']}",
+                             "decode_tok_s": (tm.generated - 1) / (tm.gpu_decode_ms / 1000.0) if tm.generated > 1 else None,
+                             "prefill_tok_s": tm.prompt_tokens / (tm.gpu_prefill_ms / 1000.0), "unit": "tok/s"}
+    return out
+
+
 def run_ours(args, ws, rank, local):
     import torch
 
@@ -306,6 +325,7 @@ def run_ours(args, ws, rank, local):
     multi = None if args.no_multi_stream else run_multi_stream(args, ws, rank, local)
     if rank != 0:
         return
+    others = run_other_configs(local) if (ws == 1 and not args.no_other_configs) else None
     K = args.steps
     value = ws * K * DECODED / (mx["dec"] / 1000.0)
     prefill = ws * K * NP / (mx["pre"] / 1000.0)
@@ -341,6 +361,8 @@ def run_ours(args, ws, rank, local):
         out["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if multi:
         out["multi_stream"] = multi
+    if others:
+        out["other_configs"] = others
     print(json.dumps(out), flush=True)
 
 
@@ -352,6 +374,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-multi-stream", action="store_true", help="skip the config 5 (64-sequence) measurement")
+    ap.add_argument("--no-other-configs", action="store_true", help="skip the single runs of configs 2-4 (N=1 only)")
     ap.add_argument("--c5-rounds", type=int, default=1, help="timed rounds of config 5")
     ap.add_argument("--c5-gen", type=int, default=0, help="greedy tokens per config 5 sequence (0: the workload's 128)")
     ap.add_argument("--only-multi-stream", action="store_true",

@@ -165,6 +165,24 @@ def test_config1_full_workload(oracle, gpus):
     assert np.array_equal(got, want), int(np.argmax(got != want))
 
 
+def test_config4_full_workload(oracle):
+    """BASELINE config 4 at full size: a 512-token prompt through 8 chunks of 64 (Qwen2.5 architecture), then
+    16 greedy tokens, token-identical; the last prompt token's logits within 1e-5 relative."""
+    path = synth.ensure("c3-qwen2.5-0.5b")
+    w = synth.WORKLOADS[4]
+    g = llm_b200.GPU(path, ctx=w["ctx"])
+    try:
+        prompt = synth.prompt_ids(g.cfg.vocab, w["prompt"], seed=4)
+        toks, logits = g.generate_logits(prompt, w["gen"])
+    finally:
+        g.close()
+    want_toks, want_logits = oracle.CPU(path, w["ctx"]).generate(prompt, w["gen"], step_logits=True)
+    assert rel_err(logits[0], want_logits[0]) <= REL_TOL
+    for i in range(w["gen"]):
+        check_step(i, logits[i], want_logits[i])
+    assert np.array_equal(toks, want_toks)
+
+
 def test_deterministic(gpus):
     g = gpus("tiny-qwen2", 256)
     prompt = synth.prompt_ids(g.cfg.vocab, 40, seed=3)
