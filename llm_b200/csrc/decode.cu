@@ -307,6 +307,11 @@ struct DecSmem {
 };
 
 // --------------------------------------------------------- dot products --
+// The activation vector is staged block by block with a stride of kXB floats
+// per 32-wide block (32 values + 4 of padding), so that 8 lanes reading 8
+// different blocks hit 8 different bank groups.
+constexpr int kXB = 36;
+
 // A tile of 8 rows in shared memory; lane (r, q) = (lane / 4, lane % 4).
 // Returns the lane's partial over blocks [b0, b1).  Everything here is on
 // the latency-critical path of a phase, so it stays in f32: double
@@ -327,8 +332,8 @@ __device__ __forceinline__ float dot_q4(const uint8_t *tile, int nb, const float
     for (int b = b0; b < b1; ++b) {
         const uint32_t w = qw[b * 32];
         const float d = __half2float(dp[b * 8]);
-        const float4 xa = reinterpret_cast<const float4 *>(xp)[b * 8 + 2 * q];
-        const float4 xb = reinterpret_cast<const float4 *>(xp)[b * 8 + 2 * q + 1];
+        const float4 xa = reinterpret_cast<const float4 *>(xp)[b * (kXB / 4) + 2 * q];
+        const float4 xb = reinterpret_cast<const float4 *>(xp)[b * (kXB / 4) + 2 * q + 1];
         const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
         float2 s = __fmul2_rn(__fadd2_rn(make_float2(b2f(lo, 0), b2f(hi, 0)), make_float2(-off2.x, -off2.y)),
                               make_float2(xa.x, xa.y));
@@ -362,8 +367,8 @@ __device__ __forceinline__ float dot_q8(const uint8_t *tile, int nb, const float
     for (int b = b0; b < b1; ++b) {
         const uint2 w = qw[b * 32];
         const float d = __half2float(dp[b * 8]);
-        const float4 xa = reinterpret_cast<const float4 *>(x)[b * 8 + 2 * q];
-        const float4 xb = reinterpret_cast<const float4 *>(x)[b * 8 + 2 * q + 1];
+        const float4 xa = reinterpret_cast<const float4 *>(x)[b * (kXB / 4) + 2 * q];
+        const float4 xb = reinterpret_cast<const float4 *>(x)[b * (kXB / 4) + 2 * q + 1];
         const uint32_t u0 = w.x ^ 0x80808080u, u1 = w.y ^ 0x80808080u;
         const float2 o2 = make_float2(-off, -off);
         float2 s = __fmul2_rn(__fadd2_rn(make_float2(b2f(u0, 0), b2f(u0, 1)), o2), make_float2(xa.x, xa.y));
@@ -382,6 +387,64 @@ __device__ __forceinline__ float dot_tile(int type, const uint8_t *tile, int nb,
     return dot_q4<false>(tile, nb, reinterpret_cast<const float2 *>(sm.xv), b0, b1, lane);
 }
 
+// Row r of a tile, one block per lane (lanes b, b + 32, ... of the nb
+// blocks), summed over the warp: every lane returns the row's value.  Used
+// for units of fewer tiles than warps, where each warp takes whole rows and
+// no partial sums cross warps.
+__device__ __forceinline__ float dot_row(int type, const uint8_t *tile, int nb, int r, const DecSmem &sm, int lane) {
+    float acc = 0.f;
+    if (type == 8) {
+        const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 256);
+        for (int b = lane; b < nb; b += 32) {
+            const uint4 *qp = reinterpret_cast<const uint4 *>(tile + ((size_t)b * 8 + r) * 32);
+            const float4 *xp = reinterpret_cast<const float4 *>(sm.xq8 + b * kXB);
+            const float d = __half2float(dp[b * 8 + r]);
+            const float2 o2 = make_float2(-8388736.f, -8388736.f);
+            float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint4 q = qp[h];
+                const uint32_t u[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const float4 x = xp[4 * h + w];
+                    s = __ffma2_rn(__fadd2_rn(make_float2(b2f(u[w], 0), b2f(u[w], 1)), o2), make_float2(x.x, x.y), s);
+                    s = __ffma2_rn(__fadd2_rn(make_float2(b2f(u[w], 2), b2f(u[w], 3)), o2), make_float2(x.z, x.w), s);
+                }
+            }
+            acc = fmaf(d, s.x + s.y, acc);
+        }
+    } else {
+        const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 128);
+        const float off = type == 3 ? 8388608.f : 8388616.f;
+        const float2 o2 = make_float2(-off, -off);
+        for (int b = lane; b < nb; b += 32) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(tile + ((size_t)b * 8 + r) * 16);
+            const float4 *xp = reinterpret_cast<const float4 *>(sm.xv + b * kXB);  // pairs (x_j, x_j+16)
+            const float d = __half2float(dp[b * 8 + r]);
+            const uint32_t wq[4] = {q.x, q.y, q.z, q.w};
+            float2 s = make_float2(0.f, 0.f), sx = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const uint32_t lo = wq[w] & 0x0F0F0F0Fu, hi = (wq[w] >> 4) & 0x0F0F0F0Fu;
+                const float4 xa = xp[2 * w], xb = xp[2 * w + 1];
+                s = __ffma2_rn(__fadd2_rn(make_float2(b2f(lo, 0), b2f(hi, 0)), o2), make_float2(xa.x, xa.y), s);
+                s = __ffma2_rn(__fadd2_rn(make_float2(b2f(lo, 1), b2f(hi, 1)), o2), make_float2(xa.z, xa.w), s);
+                s = __ffma2_rn(__fadd2_rn(make_float2(b2f(lo, 2), b2f(hi, 2)), o2), make_float2(xb.x, xb.y), s);
+                s = __ffma2_rn(__fadd2_rn(make_float2(b2f(lo, 3), b2f(hi, 3)), o2), make_float2(xb.z, xb.w), s);
+                if (type == 3)
+                    sx = __fadd2_rn(sx, __fadd2_rn(__fadd2_rn(make_float2(xa.x, xa.y), make_float2(xa.z, xa.w)),
+                                                   __fadd2_rn(make_float2(xb.x, xb.y), make_float2(xb.z, xb.w))));
+            }
+            if (type == 3) acc = fmaf(d, s.x + s.y, fmaf(__half2float(dp[(size_t)nb * 8 + b * 8 + r]), sx.x + sx.y, acc));
+            else acc = fmaf(d, s.x + s.y, acc);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+    return acc;
+}
+
 // ------------------------------------------------------------- staging --
 // Writes v (n floats, in shared memory at `src`) into the layouts the dot
 // products read: paired for Q4 (xv) and, if needed, plain for Q8 (xq8).
@@ -391,8 +454,8 @@ __device__ __forceinline__ void stage_vector(const float *src, int n, const DecS
         const float v = src[i];
         const int b = i >> 5, j = i & 31;
         const int pj = j & 15;
-        sm.xv[b * 32 + 2 * pj + (j >> 4)] = v;
-        if (q8) sm.xq8[i] = v;
+        sm.xv[b * kXB + 2 * pj + (j >> 4)] = v;
+        if (q8) sm.xq8[b * kXB + j] = v;
     }
 }
 
@@ -451,8 +514,8 @@ __device__ __forceinline__ void norm_fold(const DecParams &dm, const DecSmem &sm
         ss = fmaf(x, x, ss);
         const float v = __fmul_rn(x, sm.nrm[i]);
         const int b = i >> 5, j = i & 31, pj = j & 15;
-        sm.xv[b * 32 + 2 * pj + (j >> 4)] = v;
-        if (q8) sm.xq8[i] = v;
+        sm.xv[b * kXB + 2 * pj + (j >> 4)] = v;
+        if (q8) sm.xq8[b * kXB + j] = v;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
@@ -525,6 +588,10 @@ __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const U
             if ((lane & 3) == 0) c.rows[i * 8 + (lane >> 2)] = a;
         }
         __syncwarp();
+    } else if (k == 1) {
+        // one tile: warp w takes its row w, one block per lane, no partial sums across warps
+        const float a = dot_row(m.type, slot, m.nb, warp, sm, lane);
+        if (lane == 0) c.rows[warp] = a;
     } else {
         const int parts = kCons / k;
         const int tile = warp / parts, part = warp % parts;

@@ -147,7 +147,7 @@ struct DecLayout {
 __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int embd, int ff, int head_dim, int heads,
                                                 int gate_rows, int qkv_rows, int plan_units) {
     DecLayout l{};
-    const size_t vec = (size_t)(embd > ff ? embd : ff) * 4;
+    const size_t vec = (size_t)((embd > ff ? embd : ff) + 31) / 32 * 36 * 4;  // 32-wide blocks padded to 36 floats
     size_t p = 0;
     l.ring = p, p += (size_t)nslots * slot_bytes;
     l.full = p, p += 8 * (size_t)nslots;
