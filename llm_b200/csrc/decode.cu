@@ -1140,6 +1140,77 @@ __device__ bool ph_down(const DecParams &dm, int l, const Tok &tk, const DecSmem
 }
 
 // The head: RMSNorm(output_norm), logits, this CTA's argmax partial.
+// One unit of the head (k tiles from tile t0): logits = (W h) * nsc
+// (cpu.go:357-363), stored, and folded into this thread's running argmax.
+// With more than 4 tiles each warp takes whole tiles and the lanes holding a
+// row's value finish it, so a unit costs the slot's wait and its release;
+// with fewer, a tile's blocks are split across warps and meet in shared
+// memory first.
+__device__ __forceinline__ bool head_unit(const DecParams &dm, int k, int t0, float nsc, const DecSmem &sm, Ring &rg,
+                                          float &bv, int &bi) {
+    const QMat &m = dm.head;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sl = rg.u % rg.nslots;
+    bool ok = true;
+    if (!mbar_try_wait(sm.full + sl, (rg.u / rg.nslots) & 1)) {
+        const uint64_t t0w = gtimer();
+        while (!mbar_try_wait(sm.full + sl, (rg.u / rg.nslots) & 1)) {
+            if (read_err(dm.err)) {
+                ok = false;
+                break;
+            }
+            if (gtimer() - t0w > kWaitNs) {
+                atomicExch(dm.err, DEV_RING_TIMEOUT);
+                ok = false;
+                break;
+            }
+        }
+    }
+    if (cons_or(!ok)) return false;
+    const uint8_t *slot = sm.ring + (size_t)sl * rg.slot_bytes;
+    auto finish = [&](int tile, int r, float a) {
+        const int row = (t0 + tile) * 8 + r;
+        const float v = __fmul_rn(a, nsc);
+        if (row < dm.vocab) {
+            dm.logits[row] = v;
+            if (better(v, row, bv, bi)) bv = v, bi = row;
+        }
+    };
+    if (2 * k > kCons) {
+        for (int i = warp; i < k; i += kCons) {
+            float a = dot_tile(m.type, slot + (size_t)i * m.tile_bytes, m.nb, sm, 0, m.nb, lane);
+            a += __shfl_xor_sync(kFull, a, 1);
+            a += __shfl_xor_sync(kFull, a, 2);
+            if ((lane & 3) == 0) finish(i, lane >> 2, a);
+        }
+    } else {
+        const int parts = kCons / k;
+        const int tile = warp / parts, part = warp % parts;
+        float a = 0.f;
+        if (tile < k) {
+            const int b0 = m.nb * part / parts, b1 = m.nb * (part + 1) / parts;
+            a = dot_tile(m.type, slot + (size_t)tile * m.tile_bytes, m.nb, sm, b0, b1, lane);
+        }
+        a += __shfl_xor_sync(kFull, a, 1);
+        a += __shfl_xor_sync(kFull, a, 2);
+        float *part_s = reinterpret_cast<float *>(sm.part);
+        if ((lane & 3) == 0) part_s[(lane >> 2) * 8 + warp] = a;
+        cons_sync();
+        if (threadIdx.x < 64) {
+            float v = part_s[threadIdx.x];
+            const int w = threadIdx.x & 7;
+            if (parts >= 2) v += __shfl_xor_sync(kFull, v, 1);
+            if (parts >= 4) v += __shfl_xor_sync(kFull, v, 2);
+            if (parts >= 8) v += __shfl_xor_sync(kFull, v, 4);
+            if (w % parts == 0 && w / parts < k) finish(w / parts, threadIdx.x >> 3, v);
+        }
+    }
+    cons_sync();  // the slot (and the shared partials) are free
+    rg.u++;
+    if (threadIdx.x == kFeeder) feed_issue(sm, rg.nslots, rg.slot_bytes);
+    return true;
+}
+
 __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Share s = share(dm.head, blockIdx.x, gridDim.x, rg.slot_bytes);
     float bv = -FLT_MAX;
@@ -1153,19 +1224,8 @@ __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, R
         tk.tr.stamp(ev, 1);
         norm_fold(dm, sm, dm.head.type == 8);
         const float nsc = norm_scale(dm, sm);
-        for (int t = s.a; t < s.b; t += s.per) {
-            const int k = min(s.per, s.b - t);
-            if (!unit_rows(dm, dm.head, k, sm, rg)) return false;
-            if (threadIdx.x < k * 8) {
-                const int row = t * 8 + threadIdx.x;
-                const float v = __fmul_rn(sm.rows[threadIdx.x], nsc);
-                if (row < dm.vocab) {
-                    dm.logits[row] = v;
-                    if (better(v, row, bv, bi)) bv = v, bi = row;
-                }
-            }
-            cons_sync();
-        }
+        for (int t = s.a; t < s.b; t += s.per)
+            if (!head_unit(dm, min(s.per, s.b - t), t, nsc, sm, rg, bv, bi)) return false;
     }
     // CTA argmax over the threads that saw rows (all 8 warps reduce; idle lanes hold the identity)
     for (int o = 16; o; o >>= 1) {
@@ -1315,7 +1375,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
 }  // namespace
 
-DecConfig decode_config(const Shapes &s, int max_tile_bytes, int gate_rows, int qkv_rows, int plan_units) {
+DecConfig decode_config(const Shapes &s, int max_tile_bytes, int head_tile_bytes, int gate_rows, int qkv_rows,
+                        int plan_units) {
     // A ring of 4 slots of at least 16 KB: it runs far enough ahead of the
     // consumers, and a block of well under the 227 KB opt-in maximum leaves
     // the SM most of its L1, which holds the threads' stack and the norm and
@@ -1325,6 +1386,8 @@ DecConfig decode_config(const Shapes &s, int max_tile_bytes, int gate_rows, int 
     DecLayout base = dec_layout(0, 0, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows, plan_units);
     const int ring = budget - (int)base.total;
     int slot = max(max_tile_bytes, 16384);
+    // the head streams back to back, so a slot of 8 head tiles (when small) gives each warp a tile per unit
+    if (8 * head_tile_bytes <= 24576) slot = max(slot, 8 * head_tile_bytes);
     slot = (slot + 127) / 128 * 128;
     c.slot_bytes = slot;
     c.nslots = min(4, ring / slot);

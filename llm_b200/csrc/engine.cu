@@ -413,7 +413,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
         if (E > 1024) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports embedding sizes up to 1024"};
         if (c.head_dim != 64 && c.head_dim != 128)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel supports head sizes 64 and 128"};
-        m.dec = decode_config(s, max_tile, d.dec_gate_rows, d.dec_qkv_rows, 0);
+        m.dec = decode_config(s, max_tile, d.head.tile_bytes, d.dec_gate_rows, d.dec_qkv_rows, 0);
         if (c.layers > kMaxDecLayers) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports up to 64 layers"};
         if (m.dec.nslots < 2 || decode2_ctas_per_sm(m.dec) < 1)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel does not fit an SM (tiles of " + std::to_string(max_tile) +
@@ -441,7 +441,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
             mx = std::max(mx, v);
         }
         m.dp->feed_max = mx;
-        const DecConfig full = decode_config(s, max_tile_of(d, c.layers), d.dec_gate_rows, d.dec_qkv_rows, mx);
+        const DecConfig full = decode_config(s, max_tile_of(d, c.layers), d.head.tile_bytes, d.dec_gate_rows, d.dec_qkv_rows, mx);
         if (full.nslots != m.dec.nslots || full.slot_bytes != m.dec.slot_bytes || full.smem > 232448 ||
             decode2_ctas_per_sm(full) < 1)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel does not fit an SM with its weight plan"};

@@ -84,7 +84,8 @@ struct DecConfig {
     int nslots, slot_bytes, threads;
     size_t smem;
 };
-DecConfig decode_config(const Shapes &s, int max_tile_bytes, int gate_rows, int qkv_rows, int plan_units);
+DecConfig decode_config(const Shapes &s, int max_tile_bytes, int head_tile_bytes, int gate_rows, int qkv_rows,
+                        int plan_units);
 // Each CTA's weight units of one token for the persistent kernel (its grid: ctas).
 cudaError_t launch_feed_plan(const DecParams &dm, int slot_bytes, FeedUnit *plan, int *count, int ctas,
                              cudaStream_t st);
