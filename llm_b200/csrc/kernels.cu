@@ -60,15 +60,6 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return warp_sum(l < kWarps ? red[l] : 0.f);
 }
 
-__device__ __forceinline__ float block_max(float v, float *red) {
-    v = warp_max(v);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    __syncthreads();
-    if (l == 0) red[w] = v;
-    __syncthreads();
-    return warp_max(l < kWarps ? red[l] : -FLT_MAX);
-}
-
 // Byte k of v (0..255) plus 2^23, as a float: exact, one byte permute.
 __device__ __forceinline__ float b2f(uint32_t v, int k) {
     return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | k));
@@ -284,10 +275,14 @@ __device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bo
 // K2 + the merge of K3: attention of token t (n positions visible) for item
 // = (KV head g, chunk of kAttnChunk positions), for every query head of g's
 // GQA group (cpu.go:304-335): the chunk's K and V rows are read once into
-// shared memory and serve the group's heads; per head the scores, the chunk
-// max and exp-sum and the exp-weighted V sum (kernels_fused.go:82-146), in
-// double.  The last CTA of (token, group) to finish merges the chunks of the
-// group's heads (kernels_fused.go:150-170) into att.
+// shared memory and warp j computes query head j of the group, with no
+// barrier between its steps: lane p scores positions p and p + 32 (f32 dot
+// products, as cpu.go:311-316), the chunk max and exp-sum come from warp
+// shuffles (exp in double, rounded to f32, as cpu.go:321), then lane d sums
+// dimensions 2d, 2d + 1 of the exp-weighted V rows (kernels_fused.go:82-146).
+// The last CTA of (token, group) to finish merges the chunks of the group's
+// heads (kernels_fused.go:150-170) into att.  Groups of up to 8 query heads
+// per KV head; more take several rounds of the warps.
 __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, int item, uint32_t *att_cnt,
                            const Smem &sm) {
     const int HD = dm.head_dim, grp = dm.heads / dm.kv_heads;
@@ -297,8 +292,6 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
     float *ks = sm.vec;                          // [kAttnChunk][KS]
     float *vs = ks + kAttnChunk * KS;            // [kAttnChunk][KS]
     float *qg = vs + kAttnChunk * KS;            // [grp][HD]
-    float *e = qg + grp * HD;                    // [kAttnChunk]
-    double *dpart = reinterpret_cast<double *>(e + kAttnChunk + 2);  // kThreads * 4 doubles (8-byte aligned)
     __shared__ int last;
     const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
     const int nd4 = HD / 4;
@@ -311,60 +304,55 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
     }
     for (int i = threadIdx.x; i < grp * HD; i += kThreads) qg[i] = __ldcg(dm.q + (size_t)t * dm.embd + g * grp * HD + i);
     __syncthreads();
-    const int p = threadIdx.x >> 2, sub = threadIdx.x & 3;
-    const int G = kThreads / nd4, d4 = threadIdx.x % nd4, gi = threadIdx.x / nd4;
-    for (int j = 0; j < grp; ++j) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int j = warp; j < grp; j += kWarps) {
         const int h = g * grp + j;
         const float *qh = qg + j * HD;
-        // scores: 4 threads per position, HD/4 dims each, accumulated in double
-        float s = -FLT_MAX;
-        {
-            double part_s = 0.0;
+        float s[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int p = lane + 32 * k;
+            float a0 = 0.f, a1 = 0.f;
             if (p < cnt) {
                 const float *kr = ks + p * KS;
-                for (int d = sub * 4; d < HD; d += 16) {
+                for (int d = 0; d < HD; d += 4) {
                     const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
-                    part_s = fma((double)qh[d], (double)k4.x, part_s);
-                    part_s = fma((double)qh[d + 1], (double)k4.y, part_s);
-                    part_s = fma((double)qh[d + 2], (double)k4.z, part_s);
-                    part_s = fma((double)qh[d + 3], (double)k4.w, part_s);
+                    const float4 q4 = *reinterpret_cast<const float4 *>(qh + d);
+                    a0 = fmaf(q4.x, k4.x, a0);
+                    a1 = fmaf(q4.y, k4.y, a1);
+                    a0 = fmaf(q4.z, k4.z, a0);
+                    a1 = fmaf(q4.w, k4.w, a1);
                 }
             }
-            part_s += __shfl_xor_sync(kFull, part_s, 1);
-            part_s += __shfl_xor_sync(kFull, part_s, 2);
-            if (p < cnt) s = __fmul_rn((float)part_s, dm.scale);
+            s[k] = p < cnt ? __fmul_rn(a0 + a1, dm.scale) : -FLT_MAX;
         }
-        const float mx = block_max(s, sm.red);
-        if (p < cnt && sub == 0) e[p] = (float)exp((double)__fsub_rn(s, mx));
-        __syncthreads();
-        // V sum: thread (d4, gi): float4 d4 of the head, positions gi, gi + G, ..., in double
-        double o0 = 0, o1 = 0, o2 = 0, o3 = 0;
-        for (int pp = gi; pp < cnt; pp += G) {
-            const double w = e[pp];
-            const float4 v4 = *reinterpret_cast<const float4 *>(vs + pp * KS + d4 * 4);
-            o0 = fma(w, (double)v4.x, o0);
-            o1 = fma(w, (double)v4.y, o1);
-            o2 = fma(w, (double)v4.z, o2);
-            o3 = fma(w, (double)v4.w, o3);
+        const float mx = warp_max(fmaxf(s[0], s[1]));
+        float e[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) e[k] = lane + 32 * k < cnt ? (float)exp((double)__fsub_rn(s[k], mx)) : 0.f;
+        const float lsum = warp_sum(e[0] + e[1]);
+        // V: lane covers dimensions 2 lane, 2 lane + 1 (and 64 + 2 lane, 65 + 2 lane for head_dim 128)
+        const bool two = HD > 64;
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+        for (int p = 0; p < cnt; ++p) {
+            const float w = __shfl_sync(kFull, p < 32 ? e[0] : e[1], p & 31);
+            const float2 va = *reinterpret_cast<const float2 *>(vs + p * KS + 2 * lane);
+            o0 = fmaf(w, va.x, o0);
+            o1 = fmaf(w, va.y, o1);
+            if (two) {
+                const float2 vb = *reinterpret_cast<const float2 *>(vs + p * KS + 64 + 2 * lane);
+                o2 = fmaf(w, vb.x, o2);
+                o3 = fmaf(w, vb.y, o3);
+            }
         }
-        dpart[threadIdx.x * 4 + 0] = o0, dpart[threadIdx.x * 4 + 1] = o1;
-        dpart[threadIdx.x * 4 + 2] = o2, dpart[threadIdx.x * 4 + 3] = o3;
-        __syncthreads();
         const size_t th = (size_t)t * dm.heads + h;
-        if (threadIdx.x < nd4) {
-            double tot[4] = {0, 0, 0, 0};
-            for (int k = 0; k < G; ++k)
-                for (int q4 = 0; q4 < 4; ++q4) tot[q4] += dpart[(threadIdx.x + k * nd4) * 4 + q4];
-            for (int q4 = 0; q4 < 4; ++q4) dm.part_pv[(th * dm.nchunk + c) * HD + threadIdx.x * 4 + q4] = (float)tot[q4];
-        }
-        if (threadIdx.x == 0) {
-            double lsum = 0.0;
-            for (int pp = 0; pp < cnt; ++pp) lsum += e[pp];
-            dm.part_ml[th * dm.nchunk + c] = make_float2(mx, (float)lsum);
-        }
-        __syncthreads();  // e and dpart are reused by the next head
+        float *pv = dm.part_pv + (th * dm.nchunk + c) * HD + 2 * lane;
+        pv[0] = o0, pv[1] = o1;
+        if (two) pv[64] = o2, pv[65] = o3;
+        if (lane == 0) dm.part_ml[th * dm.nchunk + c] = make_float2(mx, lsum);
     }
     // the last arriving CTA of this (token, group) merges the group's heads
+    __syncthreads();
     const size_t tg = (size_t)t * dm.kv_heads + g;
     if (threadIdx.x == 0) {
         __threadfence();
@@ -650,9 +638,8 @@ __global__ void k_repack(const uint8_t *__restrict__ raw, int rows, int nb, int 
 
 int smem_vec_floats(const Shapes &s) {
     const int vec = s.embd + (s.embd > s.ff ? s.embd : s.ff);
-    // attention: K and V chunks, the group's queries, exp weights, double partials
-    const int attn = 2 * kAttnChunk * (s.head_dim + 4) + (s.heads / s.kv_heads) * s.head_dim + kAttnChunk + 2 +
-                     8 * kThreads;
+    // attention: K and V chunks, the group's queries
+    const int attn = 2 * kAttnChunk * (s.head_dim + 4) + (s.heads / s.kv_heads) * s.head_dim;
     return vec > attn ? vec : attn;
 }
 
