@@ -252,13 +252,12 @@ __global__ void __launch_bounds__(kGT) k_gemm(const __grid_constant__ GemmArgs g
             if (NM == 2) load_w(mb, lb, kb + 1, wb);
             load_x(ga.x, K, ga.m, kb + 1, xa, xb);
         }
-        float blk[NM][4][4];
+        // paired FMAs (two independent fused FMAs per instruction) over row pairs (c, c + 1)
+        float2 blk[NM][4][2];
 #pragma unroll
         for (int j = 0; j < NM; ++j)
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) blk[j][i][c] = 0.f;
+            for (int i = 0; i < 4; ++i) blk[j][i][0] = blk[j][i][1] = make_float2(0.f, 0.f);
 #pragma unroll 8
         for (int k = 0; k < 32; ++k) {
             const float4 a4 = *reinterpret_cast<const float4 *>(xs + k * kXS + ty * 4);
@@ -266,19 +265,22 @@ __global__ void __launch_bounds__(kGT) k_gemm(const __grid_constant__ GemmArgs g
 #pragma unroll
             for (int j = 0; j < NM; ++j) {
                 const float4 b4 = *reinterpret_cast<const float4 *>(wsm + j * 32 * kXS + k * kXS + tx * 4);
-                const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+                const float2 b01 = make_float2(b4.x, b4.y), b23 = make_float2(b4.z, b4.w);
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) blk[j][i][c] = fmaf(av[i], bv[c], blk[j][i][c]);
+                for (int i = 0; i < 4; ++i) {
+                    const float2 a2 = make_float2(av[i], av[i]);
+                    blk[j][i][0] = __ffma2_rn(a2, b01, blk[j][i][0]);
+                    blk[j][i][1] = __ffma2_rn(a2, b23, blk[j][i][1]);
+                }
             }
         }
 #pragma unroll
         for (int j = 0; j < NM; ++j)
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) acc[j][i][c] += blk[j][i][c];
+            for (int i = 0; i < 4; ++i) {
+                acc[j][i][0] += blk[j][i][0].x, acc[j][i][1] += blk[j][i][0].y;
+                acc[j][i][2] += blk[j][i][1].x, acc[j][i][3] += blk[j][i][1].y;
+            }
         __syncthreads();
     }
     if constexpr (EPI == EPI_ARGMAX) {  // no split: the tile's best row per token
