@@ -174,7 +174,10 @@ LLMB_API int llmb_set_layers(llmb_model *m, int layers);
  * "decode_mode" 0 (default) decodes with the persistent kernel, 1 with one
  * kernel per phase (an A/B and debugging aid); "prefill_mode" 0 (default)
  * runs prompt chunks and multi-stream batches through the chunked products,
- * 1 through one matvec per token and phase (the same aid); "decode_trace" 1 makes models
+ * 1 through one matvec per token and phase (the same aid); "tag_reset" N > 0
+ * clears the persistent kernel's tagged exchange buffers after every N
+ * decoded tokens (a test aid: they are cleared anyway before the 32-bit tags
+ * would wrap); "decode_trace" 1 makes models
  * opened afterwards record the persistent kernel's phase timeline, read with
  * llmb_peek(m, "trace", ...) (a profiling aid, the counterpart of GPU.Skip,
  * gpu.go:769-784).  Process-wide, like the Go package variables. */

@@ -35,7 +35,8 @@ std::atomic<int64_t> g_prefill_batch{kMaxPrefill};
 std::atomic<int64_t> g_memory_budget{0};
 std::atomic<int64_t> g_decode_mode{0};  // 0: persistent kernel, 1: per-phase kernels
 std::atomic<int64_t> g_decode_trace{0};
-std::atomic<int64_t> g_prefill_mode{0};  // 0: chunked products (gemm.cu), 1: the per-token kernels // 1: record the persistent kernel's phase timeline (read by llmb_peek "trace")
+std::atomic<int64_t> g_prefill_mode{0};
+std::atomic<int64_t> g_tag_reset{0};  // > 0: reset the decode kernel's tags after that many tokens (a test aid)  // 0: chunked products (gemm.cu), 1: the per-token kernels // 1: record the persistent kernel's phase timeline (read by llmb_peek "trace")
 
 thread_local std::string t_open_error;
 
@@ -77,6 +78,7 @@ struct Model {
     TokBatch *h_tb = nullptr;
     float *bkv = nullptr;         // multi-stream: the KV arena, bkv_slots sequences
     int bkv_slots = 0;
+    int64_t ll_tokens = 0;        // tokens the persistent kernel decoded since its tags were last reset
     // the m-token layer sequences (embedding + every layer's launches), captured once per
     // (tokens, batch or single sequence, layers) and replayed: a step of 64 sequences is ~210 launches
     std::map<int64_t, cudaGraphExec_t> graphs;
@@ -542,10 +544,36 @@ Error prefill(Model &m, int n) {
     return {LLMB_OK, ""};
 }
 
+// Zeroes the persistent kernel's tagged exchange buffers and its epoch counter
+// (stream-ordered after every launch before it).
+cudaError_t reset_tags(Model &m) {
+    const DevModel &d = m.hdm;
+    const int E = m.cfg.embd, F = m.cfg.ff, kvd = d.kvd;
+    const std::pair<void *, size_t> bufs[] = {
+        {d.ll_x, (size_t)E * 8}, {d.ll_q, (size_t)E * 8}, {d.ll_k, (size_t)kvd * 8}, {d.ll_v, (size_t)kvd * 8},
+        {d.ll_att, (size_t)E * 8}, {d.ll_act, (size_t)F * 8},
+        {d.ll_pv, (size_t)m.cfg.heads * d.nchunk * m.cfg.head_dim * 8}, {d.ll_ml, (size_t)m.cfg.heads * d.nchunk * 2 * 8},
+        {d.ll_epoch, 4}};
+    for (const auto &b : bufs) {
+        const cudaError_t e = cudaMemsetAsync(b.first, 0, b.second, m.st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 // cnt decode tokens: the persistent kernel (one launch) or the per-phase kernels.
 Error decode(Model &m, int cnt) {
     if (g_decode_mode.load() == 0) {
+        // The exchange tags are 32-bit, epoch * 8 (layers + 1) + phase: before they would wrap (about
+        // 17M tokens for 30 layers), clear the tagged buffers and restart the epoch, so that no stale
+        // word can carry a live tag.
+        const int64_t per_token = 8 * ((int64_t)m.cfg.layers + 1), forced = g_tag_reset.load();
+        if ((m.ll_tokens + cnt + 2) * per_token >= (int64_t)UINT32_MAX || (forced > 0 && m.ll_tokens >= forced)) {
+            CUDA_TRY(reset_tags(m));
+            m.ll_tokens = 0;
+        }
         CUDA_TRY(launch_decode2(*m.dp, m.dec, m.bar, cnt, m.persistent_ctas, m.st));
+        m.ll_tokens += cnt;
         m.stats.dispatches++;
     } else {
         for (int j = 0; j < cnt; j++) {
@@ -1026,6 +1054,7 @@ int llmb_set_knob(const char *name, int64_t v) {
     else if (s == "decode_mode") g_decode_mode = v ? 1 : 0;
     else if (s == "decode_trace") g_decode_trace = v ? 1 : 0;
     else if (s == "prefill_mode") g_prefill_mode = v ? 1 : 0;
+    else if (s == "tag_reset") g_tag_reset = v > 0 ? v : 0;
     else return LLMB_ERR_ARG;
     return LLMB_OK;
 }
@@ -1039,6 +1068,7 @@ int64_t llmb_get_knob(const char *name) {
     if (s == "decode_mode") return g_decode_mode;
     if (s == "decode_trace") return g_decode_trace;
     if (s == "prefill_mode") return g_prefill_mode;
+    if (s == "tag_reset") return g_tag_reset;
     return -1;
 }
 

@@ -183,6 +183,21 @@ def test_config4_full_workload(oracle):
     assert np.array_equal(toks, want_toks)
 
 
+def test_tag_reset(oracle, gpus):
+    """The decode kernel's exchange tags restart (buffers cleared, epoch 0) between launches: tokens unchanged."""
+    old = llm_b200.get_knob("tag_reset")
+    llm_b200.set_knob("tag_reset", 3)
+    try:
+        g = gpus("tiny-qwen2", 256)
+        prompt = synth.prompt_ids(g.cfg.vocab, 15, seed=9)
+        got, _ = g.generate(prompt, 40)
+        again, _ = g.generate(prompt, 40)
+    finally:
+        llm_b200.set_knob("tag_reset", old)
+    want = oracle.CPU(synth.ensure("tiny-qwen2"), 256).generate(prompt, 40)
+    assert np.array_equal(got, want) and np.array_equal(again, want)
+
+
 def test_deterministic(gpus):
     g = gpus("tiny-qwen2", 256)
     prompt = synth.prompt_ids(g.cfg.vocab, 40, seed=3)
