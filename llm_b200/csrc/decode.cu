@@ -190,11 +190,6 @@ __device__ __noinline__ bool poll_segs(const Seg (&sg)[NS], int *err) {
     return true;
 }
 
-__device__ __forceinline__ bool poll_vec(const uint64_t *src, int n, uint32_t tag, float *dst, int *err) {
-    const Seg sg[1] = {{src, n, tag, dst}};
-    return poll_segs(sg, err);
-}
-
 __device__ __forceinline__ bool poll_two(const uint64_t *a, int na, uint32_t ta, float *da, const uint64_t *b, int nb,
                                          uint32_t tb, float *db, int *err) {
     const Seg sg[2] = {{a, na, ta, da}, {b, nb, tb, db}};
@@ -523,6 +518,63 @@ __device__ __forceinline__ void norm_fold(const DecParams &dm, const DecSmem &sm
     cons_sync();
 }
 
+// The input poll of a normed phase, fused with norm_fold's staging: each
+// thread stages x * w of its word pairs into the dot products' layouts as
+// they arrive (round-based, as poll_segs) and returns its sum of squares
+// (negative on a device error).  The norm weights must be visible (waited
+// for and behind a barrier) before the call.
+__device__ __noinline__ float poll_stage(const uint64_t *src, int n, uint32_t tag, float *xv, float *xq8,
+                                         const float *nrm, int *err) {
+    const int npairs = n >> 1;
+    constexpr int K = 4;
+    float ss = 0.f;
+    for (int base = 0; base < npairs; base += K * kConsThreads) {
+        uint64_t v[2 * K];
+        unsigned pend = 0;
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+            if (base + threadIdx.x + k * kConsThreads < npairs) pend |= 1u << k;
+        const uint64_t t0 = gtimer();
+        unsigned spins = 0;
+        while (pend) {
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+                if (pend >> k & 1) ld_relaxed2(src + 2 * (base + threadIdx.x + k * kConsThreads), v[2 * k], v[2 * k + 1]);
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                if (!(pend >> k & 1)) continue;
+                if ((uint32_t)(v[2 * k] >> 32) == tag && (uint32_t)(v[2 * k + 1] >> 32) == tag) {
+                    const int i = 2 * (base + threadIdx.x + k * kConsThreads);
+                    const float x0 = __uint_as_float((uint32_t)v[2 * k]), x1 = __uint_as_float((uint32_t)v[2 * k + 1]);
+                    ss = fmaf(x1, x1, fmaf(x0, x0, ss));
+                    const float s0 = __fmul_rn(x0, nrm[i]), s1 = __fmul_rn(x1, nrm[i + 1]);
+                    const int b = i >> 5, j = i & 31;  // j even: j and j + 1 in the same block
+                    xv[b * kXB + 2 * (j & 15) + (j >> 4)] = s0;
+                    xv[b * kXB + 2 * ((j + 1) & 15) + ((j + 1) >> 4)] = s1;
+                    if (xq8) xq8[b * kXB + j] = s0, xq8[b * kXB + j + 1] = s1;
+                    pend &= ~(1u << k);
+                }
+            }
+            if (pend && (++spins & 255) == 0) {
+                if (read_err(err)) return -1.f;
+                if (gtimer() - t0 > kWaitNs) {
+                    atomicExch(err, DEV_TAG_TIMEOUT);
+                    return -1.f;
+                }
+            }
+        }
+    }
+    return ss;
+}
+
+// The warps' partial sums of squares into red[32..39] (norm_scale reads them).
+__device__ __forceinline__ void norm_sums(float ss, const DecSmem &sm) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+    if ((threadIdx.x & 31) == 0) sm.red[32 + (threadIdx.x >> 5)] = ss;
+    cons_sync();
+}
+
 // 1 / sqrt(mean of squares + eps), from norm_fold's partials (fixed order):
 // cpu.go:94 rounds 1/sqrt computed in double to float; rsqrt in double is
 // within an ulp of that double, far below float's rounding.
@@ -837,12 +889,19 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
             sm.xs[e] = v;
         }
         cons_sync();
-    } else {
-        if (cons_or(!poll_vec(dm.ll_x, E, tag_in, sm.xs, dm.err))) return false;
     }
-    tk.tr.stamp(ev, 1);
     const bool q8 = L.q.type == 8 || L.k.type == 8 || L.v.type == 8;
-    norm_fold(dm, sm, q8);
+    if (l == 0) {
+        tk.tr.stamp(ev, 1);
+        norm_fold(dm, sm, q8);
+    } else {
+        cp_async_wait_all();  // the norm weights, prefetched during the phase before
+        cons_sync();
+        const float ss = poll_stage(dm.ll_x, E, tag_in, sm.xv, q8 ? sm.xq8 : nullptr, sm.nrm, dm.err);
+        if (cons_or(ss < 0.f)) return false;
+        tk.tr.stamp(ev, 1);
+        norm_sums(ss, sm);
+    }
     const float nsc = norm_scale(dm, sm);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
     for (int t = a; t < b; ++t) {
@@ -1073,9 +1132,13 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     const int E = dm.embd, ev = l * 5 + PH_GU;
     tk.tr.stamp(ev, 0);
     const uint32_t tin = tag_of(tk.epoch, dm.layers, l, PH_O);
-    if (cons_or(!poll_vec(dm.ll_x, E, tin, sm.xs, dm.err))) return false;
+    cp_async_wait_all();  // the norm weights, prefetched during the phase before
+    cons_sync();
+    const float ss =
+        poll_stage(dm.ll_x, E, tin, sm.xv, L.gate.type == 8 || L.up.type == 8 ? sm.xq8 : nullptr, sm.nrm, dm.err);
+    if (cons_or(ss < 0.f)) return false;
     tk.tr.stamp(ev, 1);
-    norm_fold(dm, sm, L.gate.type == 8 || L.up.type == 8);
+    norm_sums(ss, sm);
     const float nsc = norm_scale(dm, sm);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_GU);
     auto swiglu = [&](int row, float g, float u) {
@@ -1220,9 +1283,12 @@ __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, R
     if (s.b > s.a) {
         const int E = dm.embd;
         const uint32_t tin = tag_of(tk.epoch, dm.layers, dm.layers - 1, PH_DOWN);
-        if (cons_or(!poll_vec(dm.ll_x, E, tin, sm.xs, dm.err))) return false;
+        cp_async_wait_all();  // the norm weights, prefetched during the phase before
+        cons_sync();
+        const float ss = poll_stage(dm.ll_x, E, tin, sm.xv, dm.head.type == 8 ? sm.xq8 : nullptr, sm.nrm, dm.err);
+        if (cons_or(ss < 0.f)) return false;
         tk.tr.stamp(ev, 1);
-        norm_fold(dm, sm, dm.head.type == 8);
+        norm_sums(ss, sm);
         const float nsc = norm_scale(dm, sm);
         for (int t = s.a; t < s.b; t += s.per)
             if (!head_unit(dm, min(s.per, s.b - t), t, nsc, sm, rg, bv, bi)) return false;
