@@ -441,19 +441,6 @@ __device__ __forceinline__ float dot_row(int type, const uint8_t *tile, int nb, 
 }
 
 // ------------------------------------------------------------- staging --
-// Writes v (n floats, in shared memory at `src`) into the layouts the dot
-// products read: paired for Q4 (xv) and, if needed, plain for Q8 (xq8).
-__device__ __forceinline__ void stage_vector(const float *src, int n, const DecSmem &sm, bool q8) {
-    const int t = threadIdx.x;
-    for (int i = t; i < n; i += kConsThreads) {
-        const float v = src[i];
-        const int b = i >> 5, j = i & 31;
-        const int pj = j & 15;
-        sm.xv[b * kXB + 2 * pj + (j >> 4)] = v;
-        if (q8) sm.xq8[b * kXB + j] = v;
-    }
-}
-
 __device__ __forceinline__ float cons_max(float v, float *red) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
@@ -565,6 +552,58 @@ __device__ __noinline__ float poll_stage(const uint64_t *src, int n, uint32_t ta
         }
     }
     return ss;
+}
+
+// The input poll of the output and down phases, fused with the staging:
+// word pairs of src0 (n0 values, tag0) are written as they arrive into the
+// dot products' layouts (xv, and xq8 unless null), those of src1 (n1 values,
+// tag1: the CTA's residual rows) into dst1.  Round-based, as poll_segs.
+__device__ __noinline__ bool poll_stage_res(const uint64_t *src0, int n0, uint32_t tag0, float *xv, float *xq8,
+                                            const uint64_t *src1, int n1, uint32_t tag1, float *dst1, int *err) {
+    const int np0 = n0 >> 1, npairs = np0 + (n1 >> 1);
+    constexpr int K = 4;
+    for (int base = 0; base < npairs; base += K * kConsThreads) {
+        uint64_t v[2 * K];
+        unsigned pend = 0;
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+            if (base + threadIdx.x + k * kConsThreads < npairs) pend |= 1u << k;
+        const uint64_t t0 = gtimer();
+        unsigned spins = 0;
+        while (pend) {
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                if (!(pend >> k & 1)) continue;
+                const int pi = base + threadIdx.x + k * kConsThreads;
+                ld_relaxed2(pi < np0 ? src0 + 2 * pi : src1 + 2 * (pi - np0), v[2 * k], v[2 * k + 1]);
+            }
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                if (!(pend >> k & 1)) continue;
+                const int pi = base + threadIdx.x + k * kConsThreads;
+                const uint32_t tag = pi < np0 ? tag0 : tag1;
+                if ((uint32_t)(v[2 * k] >> 32) != tag || (uint32_t)(v[2 * k + 1] >> 32) != tag) continue;
+                const float x0 = __uint_as_float((uint32_t)v[2 * k]), x1 = __uint_as_float((uint32_t)v[2 * k + 1]);
+                if (pi < np0) {
+                    const int i = 2 * pi, b = i >> 5, j = i & 31;  // j even: j and j + 1 in the same block
+                    xv[b * kXB + 2 * (j & 15) + (j >> 4)] = x0;
+                    xv[b * kXB + 2 * ((j + 1) & 15) + ((j + 1) >> 4)] = x1;
+                    if (xq8) xq8[b * kXB + j] = x0, xq8[b * kXB + j + 1] = x1;
+                } else {
+                    dst1[2 * (pi - np0)] = x0, dst1[2 * (pi - np0) + 1] = x1;
+                }
+                pend &= ~(1u << k);
+            }
+            if (pend && (++spins & 255) == 0) {
+                if (read_err(err)) return false;
+                if (gtimer() - t0 > kWaitNs) {
+                    atomicExch(err, DEV_TAG_TIMEOUT);
+                    return false;
+                }
+            }
+        }
+    }
+    return true;
 }
 
 // The warps' partial sums of squares into red[32..39] (norm_scale reads them).
@@ -1090,13 +1129,6 @@ __device__ bool ph_attn(const DecParams &dm, int l, const Tok &tk, int item, int
     return dm.head_dim == 128 ? ph_attn_t<128>(dm, l, tk, item, nch, sm) : ph_attn_t<64>(dm, l, tk, item, nch, sm);
 }
 
-// The attention of all heads into sm.xs (E floats), and the residual rows
-// [r0, r0 + nr) into sm.gate.
-__device__ bool gather_att(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, int r0, int nr, uint32_t xtag) {
-    const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_ATT);
-    return !cons_or(!poll_two(dm.ll_att, dm.embd, tag, sm.xs, dm.ll_x + r0, nr, xtag, sm.gate, dm.err));
-}
-
 // K3: x += Wo att (cpu.go:336-339).
 __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Layer &L = dm.layer[l];
@@ -1105,10 +1137,11 @@ __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &s
     const uint32_t tin = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
     const int ev = l * 5 + PH_O;
     tk.tr.stamp(ev, 0);
-    if (!gather_att(dm, l, tk, sm, s.a * 8, (s.b - s.a) * 8, tin)) return false;
+    const uint32_t tatt = tag_of(tk.epoch, dm.layers, l, PH_ATT);
+    if (cons_or(!poll_stage_res(dm.ll_att, dm.embd, tatt, sm.xv, L.o.type == 8 ? sm.xq8 : nullptr,
+                                dm.ll_x + s.a * 8, (s.b - s.a) * 8, tin, sm.gate, dm.err)))
+        return false;
     tk.tr.stamp(ev, 1);
-    stage_vector(sm.xs, dm.embd, sm, L.o.type == 8);
-    cons_sync();
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_O);
     for (int t = s.a; t < s.b; t += s.per) {
         const int k = min(s.per, s.b - t);
@@ -1183,11 +1216,10 @@ __device__ bool ph_down(const DecParams &dm, int l, const Tok &tk, const DecSmem
     const uint32_t tact = tag_of(tk.epoch, dm.layers, l, PH_GU), tin = tag_of(tk.epoch, dm.layers, l, PH_O);
     const int ev = l * 5 + PH_DOWN;
     tk.tr.stamp(ev, 0);
-    if (cons_or(!poll_two(dm.ll_act, F, tact, sm.xs, dm.ll_x + s.a * 8, (s.b - s.a) * 8, tin, sm.gate, dm.err)))
+    if (cons_or(!poll_stage_res(dm.ll_act, F, tact, sm.xv, L.down.type == 8 ? sm.xq8 : nullptr, dm.ll_x + s.a * 8,
+                                (s.b - s.a) * 8, tin, sm.gate, dm.err)))
         return false;
     tk.tr.stamp(ev, 1);
-    stage_vector(sm.xs, F, sm, L.down.type == 8);
-    cons_sync();
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_DOWN);
     for (int t = s.a; t < s.b; t += s.per) {
         const int k = min(s.per, s.b - t);
