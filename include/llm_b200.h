@@ -177,7 +177,11 @@ LLMB_API int llmb_set_layers(llmb_model *m, int layers);
  * 1 through one matvec per token and phase (the same aid); "tag_reset" N > 0
  * clears the persistent kernel's tagged exchange buffers after every N
  * decoded tokens (a test aid: they are cleared anyway before the 32-bit tags
- * would wrap); "decode_trace" 1 makes models
+ * would wrap); "attn_positions" N (64..256, a multiple of 32; read by
+ * llmb_open) sets the positions one attention item of the persistent kernel
+ * covers, 0 (default) as many as its shared memory holds (an A/B and test
+ * aid: longer contexts are split into items whose partials are merged);
+ * "decode_trace" 1 makes models
  * opened afterwards record the persistent kernel's phase timeline, read with
  * llmb_peek(m, "trace", ...) (a profiling aid, the counterpart of GPU.Skip,
  * gpu.go:769-784).  Process-wide, like the Go package variables. */

@@ -100,7 +100,8 @@ def _ptr(a: np.ndarray):
 
 
 def set_knob(name: str, value: int) -> None:
-    """Sets a package knob: decode_batch, prefill_batch, memory_budget, decode_mode, prefill_mode or decode_trace."""
+    """Sets a package knob: decode_batch, prefill_batch, memory_budget, decode_mode, prefill_mode, tag_reset,
+    attn_positions or decode_trace."""
     if lib().llmb_set_knob(name.encode(), int(value)) != OK:
         raise LlmError(ERR_ARG, f"llm: no knob {name!r}")
 

@@ -26,6 +26,7 @@
 // waits (bounded) for its weight copies in flight.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
 
@@ -297,7 +298,7 @@ struct DecSmem {
     float *att;              // attention scratch
     float *merge;            // attention partials of up to 8 chunks: pv [8][E], then (max, sum) [8][H]
     float *pre;              // the QKV epilogue's bias and RoPE (cos, sin) per row of the CTA's share
-    float *kvs;              // an attention item's history K and V rows [2][kAttnChunk][head_dim]
+    float *kvs;              // an attention item's history K and V rows [2][dec_chunk][head_dim] (aliases xv..gate)
     float *nrm;              // the next norm's weights (embd floats)
 };
 
@@ -441,19 +442,6 @@ __device__ __forceinline__ float dot_row(int type, const uint8_t *tile, int nb, 
 }
 
 // ------------------------------------------------------------- staging --
-__device__ __forceinline__ float cons_max(float v, float *red) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    cons_sync();
-    if (l == 0) red[w] = v;
-    cons_sync();
-    float t = l < kCons ? red[l] : -FLT_MAX;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) t = fmaxf(t, __shfl_xor_sync(kFull, t, o));
-    return t;
-}
-
 // Asynchronous global -> shared copies (cp.async): the issuing thread does not
 // wait for them; cp_async_wait_all waits for all of the thread's copies.
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
@@ -978,36 +966,50 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
 }
 
 // K2: attention of the token (n = pos + 1 positions) for item (head,
-// chunk of kAttnChunk positions): scores, the chunk's max and sum of exp, the
+// chunk of dm.dec_chunk positions): scores, max and sum of exp, the
 // exp-weighted V sum (kernels_fused.go:82-146).  The chunk's cached K and V
 // rows do not depend on this token, so they are copied into shared memory
-// (cp.async) before the item waits for the token's q, k, v.  With one chunk
-// the item writes the head's output; otherwise its partial, chunk-major
-// (ll_pv[c][h][d], ll_ml[c][h][{max, sum}]), for the output projection to
-// merge.  f32 arithmetic, the exp in double as cpu.go:321.
+// (cp.async) before the item waits for the token's q, k, v.  Each warp takes
+// a contiguous share of the positions, a lane per position for the scores
+// and a lane per HD/32 dimensions for the V sum, with its own max; the eight
+// warp partials are then combined.  With one chunk the item writes the
+// head's output; otherwise the item holding the current position merges the
+// others' partials.  f32 arithmetic (the exp in double in cpu.go:321: within
+// 2 ulp), the merge of chunks in double.
+//
+// K/V rows sit in shared memory at a stride of HD floats with their 16-byte
+// groups permuted (group g of row p at g ^ (p & 15)): a quarter warp reading
+// the same group of 8 consecutive rows, or a warp reading one row, touches
+// each bank once.
+template <int HD>
+__device__ __forceinline__ int kv_swz(int p, int d) {
+    return p * HD + ((((d >> 2) ^ (p & 15))) << 2) + (d & 3);
+}
+
 template <int HD>
 __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, int nch, const DecSmem &sm) {
-    constexpr int KS = HD + 16;  // shared row stride: conflict-free 4-threads-per-row reads
     constexpr int V4 = HD / 4;
+    constexpr int VD = HD / 32;  // V dimensions per lane
     const int grp = dm.heads / dm.kv_heads;
     const int h = item / nch, c = item % nch, kvh = h / grp;
-    const int n = tk.pos + 1;
+    const int n = tk.pos + 1, C = dm.dec_chunk;
     const Layer &L = dm.layer[l];
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
     const uint32_t otag = tag_of(tk.epoch, dm.layers, l, PH_ATT);
-    float *qh = sm.att, *kc = sm.att + HD, *vc = sm.att + 2 * HD, *e = sm.att + 3 * HD;
-    float *part = sm.att + 3 * HD + kAttnChunk;  // kConsThreads x 4 floats
-    float *ks = sm.kvs, *vs = sm.kvs + kAttnChunk * KS;
-    const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
+    float *qh = sm.att, *kc = sm.att + HD, *vc = sm.att + 2 * HD;
+    float *wpart = sm.att + 3 * HD;  // [8 warps][HD + 4]: V sum, then max and sum of exp
+    float *ks = sm.kvs, *vs = sm.kvs + (size_t)C * HD;
+    const int p0 = c * C, cnt = min(C, n - p0);
     const bool has_cur = p0 + cnt == n;
     const int nhist = has_cur ? cnt - 1 : cnt;
     const int ev = l * 5 + PH_ATT;
     tk.tr.stamp(ev, 0);
+    cons_sync();  // the K/V rows share their bytes with the previous phase's vectors
     for (int i = threadIdx.x; i < nhist * V4; i += kConsThreads) {
         const int p = i / V4, d4 = i % V4;
         const size_t row = (size_t)(p0 + p) * dm.kvd + kvh * HD + d4 * 4;
-        cp_async16(ks + p * KS + d4 * 4, L.kv + row);
-        cp_async16(vs + p * KS + d4 * 4, L.kv + (size_t)dm.ctx * dm.kvd + row);
+        cp_async16(ks + kv_swz<HD>(p, d4 * 4), L.kv + row);
+        cp_async16(vs + kv_swz<HD>(p, d4 * 4), L.kv + (size_t)dm.ctx * dm.kvd + row);
     }
     const int ncur = has_cur ? HD : 0;
     const Seg qkv[3] = {{dm.ll_q + h * HD, HD, tag, qh}, {dm.ll_k + kvh * HD, ncur, tag, kc},
@@ -1016,79 +1018,84 @@ __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, i
     cp_async_wait_all();
     if (cons_or(!ok)) return false;
     tk.tr.stamp(ev, 1);
-    if (has_cur)
-        for (int i = threadIdx.x; i < HD; i += kConsThreads) ks[nhist * KS + i] = kc[i], vs[nhist * KS + i] = vc[i];
-    cons_sync();
-    // scores: 4 threads per position; thread sub reads float4s sub, sub + 4, ...
-    const int p = threadIdx.x >> 2, sub = threadIdx.x & 3;
-    float s = -FLT_MAX;
-    {
-        float ps0 = 0.f, ps1 = 0.f;
-        if (p < cnt) {
-#pragma unroll
-            for (int j = 0; j < HD / 16; ++j) {
-                const int d = 4 * (sub + 4 * j);
-                const float4 k4 = *reinterpret_cast<const float4 *>(ks + p * KS + d);
-                const float4 q4 = *reinterpret_cast<const float4 *>(qh + d);
-                ps0 = fmaf(q4.x, k4.x, ps0);
-                ps1 = fmaf(q4.y, k4.y, ps1);
-                ps0 = fmaf(q4.z, k4.z, ps0);
-                ps1 = fmaf(q4.w, k4.w, ps1);
-            }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int per = (cnt + kCons - 1) / kCons;  // positions per warp (at most 32)
+    const int wp0 = warp * per, wcnt = max(0, min(per, cnt - wp0));
+    // scores: a lane per position (the current one's K row is kc, unpermuted)
+    float sc = -FLT_MAX;
+    if (lane < wcnt) {
+        const int p = wp0 + lane;
+        const bool cur = p == nhist;
+        const float *kr = cur ? kc : ks + (size_t)p * HD;
+        const int sw = cur ? 0 : (p & 15);
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 4
+        for (int g = 0; g < V4; ++g) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(kr + ((g ^ sw) << 2));
+            const float4 q4 = *reinterpret_cast<const float4 *>(qh + 4 * g);
+            a0 = fmaf(q4.x, k4.x, a0);
+            a1 = fmaf(q4.y, k4.y, a1);
+            a2 = fmaf(q4.z, k4.z, a2);
+            a3 = fmaf(q4.w, k4.w, a3);
         }
-        float ps = ps0 + ps1;
-        ps += __shfl_xor_sync(kFull, ps, 1);
-        ps += __shfl_xor_sync(kFull, ps, 2);
-        if (p < cnt) s = __fmul_rn(ps, dm.scale);
+        sc = __fmul_rn((a0 + a1) + (a2 + a3), dm.scale);
     }
-    const float mx = cons_max(s, sm.red);
-    if (p < cnt && sub == 0) e[p] = expf(__fsub_rn(s, mx));  // cpu.go:321 (exp in double there: within 2 ulp)
-    cons_sync();
-    constexpr int G = kConsThreads / V4;
-    const int d4 = threadIdx.x % V4, g = threadIdx.x / V4;
-    float o0 = 0, o1 = 0, o2 = 0, o3 = 0;
+    float mx = sc;
 #pragma unroll
-    for (int k = 0; k < kAttnChunk / G; ++k) {
-        const int pp = g + k * G;
-        if (pp < cnt) {
-            const float w = e[pp];
-            const float4 v4 = *reinterpret_cast<const float4 *>(vs + pp * KS + d4 * 4);
-            o0 = fmaf(w, v4.x, o0);
-            o1 = fmaf(w, v4.y, o1);
-            o2 = fmaf(w, v4.z, o2);
-            o3 = fmaf(w, v4.w, o3);
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    const float e = lane < wcnt ? expf(__fsub_rn(sc, mx)) : 0.f;  // cpu.go:321
+    float ls = e;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(kFull, ls, o);
+    float ov[VD];
+#pragma unroll
+    for (int k = 0; k < VD; ++k) ov[k] = 0.f;
+    for (int j = 0; j < wcnt; ++j) {
+        const float w = __shfl_sync(kFull, e, j);
+        const int p = wp0 + j;
+        const bool cur = p == nhist;
+        const float *vr = cur ? vc + VD * lane : vs + kv_swz<HD>(p, VD * lane);
+        if constexpr (VD == 2) {
+            const float2 v2 = *reinterpret_cast<const float2 *>(vr);
+            ov[0] = fmaf(w, v2.x, ov[0]);
+            ov[1] = fmaf(w, v2.y, ov[1]);
+        } else {
+            const float4 v4 = *reinterpret_cast<const float4 *>(vr);
+            ov[0] = fmaf(w, v4.x, ov[0]);
+            ov[1] = fmaf(w, v4.y, ov[1]);
+            ov[2] = fmaf(w, v4.z, ov[2]);
+            ov[3] = fmaf(w, v4.w, ov[3]);
         }
     }
-    part[threadIdx.x * 4 + 0] = o0, part[threadIdx.x * 4 + 1] = o1;
-    part[threadIdx.x * 4 + 2] = o2, part[threadIdx.x * 4 + 3] = o3;
+    float *wp = wpart + warp * (HD + 4);
+#pragma unroll
+    for (int k = 0; k < VD; ++k) wp[VD * lane + k] = ov[k];
+    if (lane == 0) wp[HD] = mx, wp[HD + 1] = ls;
     cons_sync();
+    // the warps' partials combined: thread d < HD sums dimension d
     float *own = sm.merge;  // the merging item's own partial: V sum [HD], max, sum of exp
-    float lsum = 0.f;
-    if (threadIdx.x < 32) {
-        lsum = (threadIdx.x < cnt ? e[threadIdx.x] : 0.f) + (threadIdx.x + 32 < cnt ? e[threadIdx.x + 32] : 0.f);
+    const int d = threadIdx.x;
+    float cm = -FLT_MAX, cl = 0.f, co = 0.f;
+    if (d < HD) {
 #pragma unroll
-        for (int o = 16; o; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
-    }
-    if (threadIdx.x < V4) {
-        float t4[4] = {0, 0, 0, 0};
+        for (int w = 0; w < kCons; ++w) cm = fmaxf(cm, wpart[w * (HD + 4) + HD]);
 #pragma unroll
-        for (int k = 0; k < G; ++k)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) t4[j] += part[(threadIdx.x + k * V4) * 4 + j];
-        const size_t pi = (size_t)h * dm.nchunk + c;  // head-major: a head's chunks are contiguous
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int d = threadIdx.x * 4 + j;
-            if (nch == 1) ll_put(dm.ll_att + h * HD + d, __fdiv_rn(t4[j], lsum), otag);
-            else if (has_cur) own[d] = t4[j];
-            else ll_put(dm.ll_pv + pi * HD + d, t4[j], otag);
+        for (int w = 0; w < kCons; ++w) {
+            const float *pw = wpart + w * (HD + 4);
+            const float f = pw[HD + 1] > 0.f ? expf(__fsub_rn(pw[HD], cm)) : 0.f;
+            cl = fmaf(f, pw[HD + 1], cl);
+            co = fmaf(f, pw[d], co);
         }
-        if (nch > 1 && threadIdx.x == 0) {
+        const size_t pi = (size_t)h * dm.nchunk + c;  // head-major: a head's chunks are contiguous
+        if (nch == 1) ll_put(dm.ll_att + h * HD + d, __fdiv_rn(co, cl), otag);
+        else if (has_cur) own[d] = co;
+        else ll_put(dm.ll_pv + pi * HD + d, co, otag);
+        if (nch > 1 && d == 0) {
             if (has_cur) {
-                own[HD] = mx, own[HD + 1] = lsum;
+                own[HD] = cm, own[HD + 1] = cl;
             } else {
-                ll_put(dm.ll_ml + pi * 2, mx, otag);
-                ll_put(dm.ll_ml + pi * 2 + 1, lsum, otag);
+                ll_put(dm.ll_ml + pi * 2, cm, otag);
+                ll_put(dm.ll_ml + pi * 2 + 1, cl, otag);
             }
         }
     }
@@ -1387,7 +1394,7 @@ __device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *
             if (threadIdx.x == 0) atomicExch(dm.err, DEV_CONTEXT_FULL);
             return;
         }
-        const int nch = (tk.pos + 1 + kAttnChunk - 1) / kAttnChunk;
+        const int nch = (tk.pos + dm.dec_chunk) / dm.dec_chunk;
         tk.tr.p = (dm.trace && i == 0) ? dm.trace + (size_t)blockIdx.x * dm.trace_events * 4 : nullptr;
         if (threadIdx.x == 0) s_ring_wait = 0;
         if (blockIdx.x == 0) {  // the embedding row is the residual of layer 0
@@ -1405,7 +1412,9 @@ __device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *
         qkv_prefetch(dm, 0, tk, sm);
         for (int l = 0; l < dm.layers; ++l) {
             if (!ph_qkv(dm, l, tk, sm, rg)) return;
-            for (int item = blockIdx.x; item < dm.heads * nch; item += gridDim.x)
+            // attention items from the last CTA down: those have no QKV, output
+            // or down rows, so they copy the K/V history well before q, k, v arrive
+            for (int item = gridDim.x - 1 - blockIdx.x; item < dm.heads * nch; item += gridDim.x)
                 if (!ph_attn(dm, l, tk, item, nch, sm)) return;
             prefetch_norm(dm.layer[l].ffn_norm, dm.embd, sm);
             if (!ph_o(dm, l, tk, sm, rg)) return;
@@ -1437,7 +1446,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     {
         const DecLayout lo =
             dec_layout(nslots, slot_bytes, dm.embd, dm.ff, dm.head_dim, dm.heads, dm.dec_gate_rows, dm.dec_qkv_rows,
-                       dm.feed_max);
+                       dm.feed_max, dm.dec_chunk);
         sm.ring = dsm + lo.ring;
         sm.full = reinterpret_cast<uint64_t *>(dsm + lo.full);
         sm.feed = reinterpret_cast<Feed *>(dsm + lo.feed);
@@ -1474,22 +1483,38 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 }  // namespace
 
 DecConfig decode_config(const Shapes &s, int max_tile_bytes, int head_tile_bytes, int gate_rows, int qkv_rows,
-                        int plan_units) {
+                        int plan_units, int attn_positions) {
     // A ring of 4 slots of at least 16 KB: it runs far enough ahead of the
     // consumers, and a block of well under the 227 KB opt-in maximum leaves
     // the SM most of its L1, which holds the threads' stack and the norm and
     // RoPE rows each phase reads (with the maximum, this kernel ran 5 % slower).
     DecConfig c{};
     const int budget = 232448 - 8192;  // the opt-in maximum per block, less margin
-    DecLayout base = dec_layout(0, 0, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows, plan_units);
-    const int ring = budget - (int)base.total;
+    auto total = [&](int nslots, int slot, int chunk) {
+        return dec_layout(nslots, slot, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows, plan_units, chunk).total;
+    };
+    const int ring = budget - (int)total(0, 0, 64);
     int slot = max(max_tile_bytes, 16384);
     // the head streams back to back, so a slot of 8 head tiles (when small) gives each warp a tile per unit
     if (8 * head_tile_bytes <= 24576) slot = max(slot, 8 * head_tile_bytes);
     slot = (slot + 127) / 128 * 128;
     c.slot_bytes = slot;
     c.nslots = min(4, ring / slot);
-    c.smem = dec_layout(c.nslots, c.slot_bytes, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows, plan_units).total;
+    // Positions per attention item: a head's whole context in one item when
+    // it fits saves the exchange of partials between CTAs.  By default the
+    // most (a multiple of 32, at most 256: a lane per position of a warp's
+    // share) for which the block stays within the 196 KB shared-memory
+    // carveout, less the 1 KB the runtime reserves per block, or within the
+    // size it has with 64 positions.
+    const size_t cap = attn_positions > 0 ? (size_t)budget
+                                          : std::max<size_t>(total(c.nslots, slot, 64), 196 * 1024 - 1024);
+    c.chunk = 64;
+    for (int k = attn_positions > 0 ? attn_positions : 256; k > 64; k -= 32)
+        if (total(c.nslots, slot, k) <= cap) {
+            c.chunk = k;
+            break;
+        }
+    c.smem = total(c.nslots, slot, c.chunk);
     c.threads = kDecThreads;
     return c;
 }

@@ -109,6 +109,7 @@ struct ModelHeader {
     uint32_t *ll_epoch;  // tokens decoded so far by the persistent kernel (makes tags unique across calls)
     int dec_gate_rows;   // gate rows of the largest gate/up share of a CTA
     int dec_qkv_rows;    // rows of the largest QKV share of a CTA
+    int dec_chunk;       // positions per attention item (a multiple of 32, 64..256)
     // each CTA's units of one token, in consumption order (plan[cta * kMaxFeedPlan + j],
     // feed_count[cta] of them; feed_max the largest count), built once per model
     const FeedUnit *feed_plan;
@@ -145,7 +146,7 @@ struct DecLayout {
 };
 
 __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int embd, int ff, int head_dim, int heads,
-                                                int gate_rows, int qkv_rows, int plan_units) {
+                                                int gate_rows, int qkv_rows, int plan_units, int dec_chunk) {
     DecLayout l{};
     const size_t vec = (size_t)((embd > ff ? embd : ff) + 31) / 32 * 36 * 4;  // 32-wide blocks padded to 36 floats
     size_t p = 0;
@@ -160,15 +161,19 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     l.part = p, p += 8 * 64;
     l.rows = p, p += 4 * 256;
     l.gate = p, p += 4 * (size_t)gate_rows;
+    // an attention item's history K and V rows [2][dec_chunk][head_dim] share
+    // the bytes of the matrix phases' vectors above (no phase uses both)
+    l.kvs = l.xv;
+    const size_t kv_end = l.kvs + 4 * (size_t)2 * dec_chunk * head_dim;
+    p = p > kv_end ? p : kv_end;
     p = (p + 15) / 16 * 16;
     l.red = p, p += 4 * 64;
-    l.att = p, p += 4 * (size_t)(3 * head_dim + 64) + 8 * 4 * 256;
+    l.att = p, p += 4 * (size_t)(3 * head_dim + 8 * (head_dim + 4));
     p = (p + 15) / 16 * 16;
     l.merge = p, p += 4 * (size_t)(9 * head_dim + 32);
     p = (p + 15) / 16 * 16;
     l.pre = p, p += 4 * (size_t)(4 * qkv_rows);
-    p = (p + 127) / 128 * 128;
-    l.kvs = p, p += 4 * (size_t)(2 * 64 * (head_dim + 16));
+    p = (p + 15) / 16 * 16;
     l.nrm = p, p += 4 * (size_t)embd;
     l.total = (p + 127) / 128 * 128;
     return l;

@@ -34,9 +34,10 @@ std::atomic<int64_t> g_decode_batch{8};
 std::atomic<int64_t> g_prefill_batch{kMaxPrefill};
 std::atomic<int64_t> g_memory_budget{0};
 std::atomic<int64_t> g_decode_mode{0};  // 0: persistent kernel, 1: per-phase kernels
-std::atomic<int64_t> g_decode_trace{0};
-std::atomic<int64_t> g_prefill_mode{0};
-std::atomic<int64_t> g_tag_reset{0};  // > 0: reset the decode kernel's tags after that many tokens (a test aid)  // 0: chunked products (gemm.cu), 1: the per-token kernels // 1: record the persistent kernel's phase timeline (read by llmb_peek "trace")
+std::atomic<int64_t> g_decode_trace{0};  // 1: record the persistent kernel's phase timeline (llmb_peek "trace")
+std::atomic<int64_t> g_prefill_mode{0};   // 0: chunked products (gemm.cu), 1: the per-token kernels
+std::atomic<int64_t> g_tag_reset{0};      // > 0: reset the decode kernel's tags after that many tokens (a test aid)
+std::atomic<int64_t> g_attn_positions{0}; // positions per attention item of the decode kernel (0: as many as fit)
 
 thread_local std::string t_open_error;
 
@@ -415,7 +416,9 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
         if (E > 1024) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports embedding sizes up to 1024"};
         if (c.head_dim != 64 && c.head_dim != 128)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel supports head sizes 64 and 128"};
-        m.dec = decode_config(s, max_tile, d.head.tile_bytes, d.dec_gate_rows, d.dec_qkv_rows, 0);
+        m.dec = decode_config(s, max_tile, d.head.tile_bytes, d.dec_gate_rows, d.dec_qkv_rows, 0,
+                              (int)g_attn_positions.load());
+        d.dec_chunk = m.dec.chunk;
         if (c.layers > kMaxDecLayers) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports up to 64 layers"};
         if (m.dec.nslots < 2 || decode2_ctas_per_sm(m.dec) < 1)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel does not fit an SM (tiles of " + std::to_string(max_tile) +
@@ -443,11 +446,13 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
             mx = std::max(mx, v);
         }
         m.dp->feed_max = mx;
-        const DecConfig full = decode_config(s, max_tile_of(d, c.layers), d.head.tile_bytes, d.dec_gate_rows, d.dec_qkv_rows, mx);
+        const DecConfig full = decode_config(s, max_tile_of(d, c.layers), d.head.tile_bytes, d.dec_gate_rows,
+                                             d.dec_qkv_rows, mx, (int)g_attn_positions.load());
         if (full.nslots != m.dec.nslots || full.slot_bytes != m.dec.slot_bytes || full.smem > 232448 ||
             decode2_ctas_per_sm(full) < 1)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel does not fit an SM with its weight plan"};
         m.dec = full;
+        m.dp->dec_chunk = full.chunk;
     }
     CUDA_TRY(cudaHostAlloc(&m.h_tokens, (size_t)(ctx + 2 * kMaxDecodeBatch + 1) * 4, cudaHostAllocDefault));
     CUDA_TRY(cudaHostAlloc(&m.h_state, 16, cudaHostAllocDefault));
@@ -1055,6 +1060,7 @@ int llmb_set_knob(const char *name, int64_t v) {
     else if (s == "decode_trace") g_decode_trace = v ? 1 : 0;
     else if (s == "prefill_mode") g_prefill_mode = v ? 1 : 0;
     else if (s == "tag_reset") g_tag_reset = v > 0 ? v : 0;
+    else if (s == "attn_positions") g_attn_positions = v > 0 ? std::clamp<int64_t>(v, 64, 256) / 32 * 32 : 0;
     else return LLMB_ERR_ARG;
     return LLMB_OK;
 }
@@ -1069,6 +1075,7 @@ int64_t llmb_get_knob(const char *name) {
     if (s == "decode_trace") return g_decode_trace;
     if (s == "prefill_mode") return g_prefill_mode;
     if (s == "tag_reset") return g_tag_reset;
+    if (s == "attn_positions") return g_attn_positions;
     return -1;
 }
 

@@ -81,11 +81,11 @@ void launch_advance(const DevModel *dm, int n, cudaStream_t st);
 
 // The warp-specialised persistent decode kernel (decode.cu).
 struct DecConfig {
-    int nslots, slot_bytes, threads;
+    int nslots, slot_bytes, threads, chunk;  // chunk: positions per attention item
     size_t smem;
 };
 DecConfig decode_config(const Shapes &s, int max_tile_bytes, int head_tile_bytes, int gate_rows, int qkv_rows,
-                        int plan_units);
+                        int plan_units, int attn_positions);
 // Each CTA's weight units of one token for the persistent kernel (its grid: ctas).
 cudaError_t launch_feed_plan(const DecParams &dm, int slot_bytes, FeedUnit *plan, int *count, int ctas,
                              cudaStream_t st);

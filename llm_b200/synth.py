@@ -68,8 +68,10 @@ TINY_LLAMA = Spec("tiny-llama", 11, "llama", 256, 3, 4, 2, 512, 1024, 1e4, 1e-5)
 TINY_MIXED = Spec("tiny-mixed", 12, "llama", 256, 3, 4, 1, 512, 1024, 1e4, 1e-5,
                   emb_type=T_Q8_0, out_type=T_Q8_0, types={"attn_v": T_Q4_1, "ffn_down": T_Q4_1})
 TINY_QWEN = Spec("tiny-qwen2", 13, "qwen2", 384, 3, 6, 2, 768, 1536, 1e6, 1e-6, out_type=T_Q8_0)
+# head_dim 128 (the other supported head size)
+TINY_HD128 = Spec("tiny-hd128", 14, "llama", 512, 2, 4, 2, 1024, 1024, 1e4, 1e-5)
 
-SPECS = {s.name: s for s in (C1, C2, C3, TINY_LLAMA, TINY_MIXED, TINY_QWEN)}
+SPECS = {s.name: s for s in (C1, C2, C3, TINY_LLAMA, TINY_MIXED, TINY_QWEN, TINY_HD128)}
 
 # The five BASELINE.json configurations: which file, prompt length, greedy tokens, context.
 WORKLOADS = {

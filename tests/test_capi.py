@@ -36,7 +36,8 @@ def test_library_exports_every_declared_symbol():
 
 def test_knobs():
     """DecodeBatch clamps to 1..MaxBatch (gpu.go:1046,1054), PrefillBatch to 1..64."""
-    old = {k: llm_b200.get_knob(k) for k in ("decode_batch", "prefill_batch", "memory_budget", "decode_mode")}
+    old = {k: llm_b200.get_knob(k) for k in ("decode_batch", "prefill_batch", "memory_budget", "decode_mode",
+                                              "attn_positions")}
     try:
         llm_b200.set_knob("decode_batch", 100)
         assert llm_b200.get_knob("decode_batch") == 16
@@ -44,6 +45,12 @@ def test_knobs():
         assert llm_b200.get_knob("decode_batch") == 1
         llm_b200.set_knob("prefill_batch", 1000)
         assert llm_b200.get_knob("prefill_batch") == 64
+        llm_b200.set_knob("attn_positions", 100)
+        assert llm_b200.get_knob("attn_positions") == 96
+        llm_b200.set_knob("attn_positions", 1000)
+        assert llm_b200.get_knob("attn_positions") == 256
+        llm_b200.set_knob("attn_positions", 0)
+        assert llm_b200.get_knob("attn_positions") == 0
         with pytest.raises(llm_b200.LlmError):
             llm_b200.set_knob("tpr", 8)
         assert llm_b200.get_knob("nothing") == -1

@@ -156,6 +156,41 @@ def test_benchmark_models_every_step(oracle, gpus, spec, n_prompt, n):
     assert np.array_equal(toks, want_toks)
 
 
+@pytest.mark.parametrize("n_prompt", [5, 150])
+def test_head_dim_128(oracle, gpus, decode_mode, n_prompt):
+    """A model with 128-wide heads: prefill and every decoded step against the oracle."""
+    g = gpus("tiny-hd128", 512)
+    prompt = synth.prompt_ids(g.cfg.vocab, n_prompt, seed=31)
+    n = 24
+    want_toks, want_logits = oracle.CPU(synth.ensure("tiny-hd128"), 512).generate(prompt, n, step_logits=True)
+    toks, logits = g.generate_logits(prompt, n)
+    for i in range(n):
+        check_step(i, logits[i], want_logits[i])
+    assert np.array_equal(toks, want_toks)
+
+
+@pytest.mark.parametrize("spec,positions", [("tiny-qwen2", 64), ("tiny-qwen2", 96), ("tiny-qwen2", 256),
+                                            ("tiny-hd128", 64)])
+def test_attention_positions(oracle, spec, positions):
+    """The decode kernel's attention items of 64, 96 or 256 positions (knob attn_positions): with the shorter
+    ones a head's context spans several items whose partials are merged.  Every step against the oracle."""
+    old = llm_b200.get_knob("attn_positions")
+    llm_b200.set_knob("attn_positions", positions)
+    try:
+        g = llm_b200.GPU(synth.ensure(spec), ctx=512)
+    finally:
+        llm_b200.set_knob("attn_positions", old)
+    try:
+        prompt = synth.prompt_ids(g.cfg.vocab, 150, seed=positions)
+        toks, logits = g.generate_logits(prompt, 40)
+    finally:
+        g.close()
+    want_toks, want_logits = oracle.CPU(synth.ensure(spec), 512).generate(prompt, 40, step_logits=True)
+    for i in range(40):
+        check_step(i, logits[i], want_logits[i])
+    assert np.array_equal(toks, want_toks)
+
+
 def test_config1_full_workload(oracle, gpus):
     """BASELINE config 1 at full size: 128 prompt tokens, 128 greedy tokens, token-identical."""
     g = gpus("c1-smollm2-q4_0", 512)
