@@ -267,13 +267,18 @@ struct Share {
     int a, b, per;
 };
 
+// floor(T * i / P) for the split of T tiles over P CTAs: 32-bit unsigned
+// arithmetic (T * P stays far below 2^32), since a 64-bit division is a
+// long dependent sequence that sat at the head of every phase.
+__device__ __forceinline__ int split_at(int T, int i, int P) { return (int)((unsigned)T * (unsigned)i / (unsigned)P); }
+
 __device__ __forceinline__ Share share(const QMat &m, int cta, int ncta, int slot_bytes) {
     const int T = m.rows >> 3;
     const int P = min(ncta, T);
     Share s;
     if (cta < P) {
-        s.a = (int)((int64_t)T * cta / P);
-        s.b = (int)((int64_t)T * (cta + 1) / P);
+        s.a = split_at(T, cta, P);
+        s.b = split_at(T, cta + 1, P);
     } else {
         s.a = s.b = 0;
     }
@@ -287,6 +292,7 @@ struct DecSmem {
     uint64_t *full;          // ring mbarriers (one per slot)
     struct Feed *feed;       // the feeder thread's cursor
     FeedUnit *plan;          // the CTA's units of one token
+    Layer *lay;              // descriptors of the current and the next two layers (buffer g % 3, g = layers so far)
     uint8_t *ring;           // nslots * slot_bytes
     float *xv;               // activation vector, paired layout for Q4 / plain for Q8 (max(E,F) floats)
     float *xq8;              // the same vector in plain layout when a Q8_0 matrix reads it
@@ -298,7 +304,7 @@ struct DecSmem {
     float *att;              // attention scratch
     float *merge;            // attention partials of up to 8 chunks: pv [8][E], then (max, sum) [8][H]
     float *pre;              // the QKV epilogue's bias and RoPE (cos, sin) per row of the CTA's share
-    float *kvs;              // an attention item's history K and V rows [2][dec_chunk][head_dim] (aliases xv..gate)
+    float *kvs;              // an attention item's history K rows, then V rows (aliases xv..gate)
     float *nrm;              // the next norm's weights (embd floats)
 };
 
@@ -772,7 +778,7 @@ __device__ bool feed_next(const DecParams &dm, Feed &f, int ntok, int slot_bytes
             const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, T = nq + nk + (L.v.rows >> 3);
             const int P = min(ncta, T);
             if (cta < P) {
-                const int a = (int)((int64_t)T * cta / P), b = (int)((int64_t)T * (cta + 1) / P);
+                const int a = split_at(T, cta, P), b = split_at(T, cta + 1, P);
                 const int t = a + f.t;
                 if (t < b) {
                     const QMat &m = t < nq ? L.q : t < nq + nk ? L.k : L.v;
@@ -862,21 +868,36 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { retur
 struct Tok {
     int pos, step, tok;
     uint32_t epoch;
+    int g0;    // layers of the launch before this token's (indexes the descriptor buffers)
     Trace tr;  // this token's timeline (first token of a launch only)
 };
+
+// Per-layer descriptors are read from shared memory: the kernel parameter's
+// copy sits in the constant bank, where the first read of a layer's fields in
+// a phase missed the constant cache (a few hundred ns at every phase).  Layer
+// g % layers of the launch's sequence goes to buffer g % 3, copied two layers
+// ahead (cp.async) and waited for at the top of the layer before it.
+__device__ __forceinline__ const Layer &lay(const DecSmem &sm, const Tok &tk, int l) { return sm.lay[(tk.g0 + l) % 3]; }
+
+__device__ __forceinline__ void fetch_layer(const DecParams &dm, const DecSmem &sm, int g) {
+    constexpr int NP = (int)(sizeof(Layer) / 16);
+    if (threadIdx.x < NP)
+        cp_async16(reinterpret_cast<char *>(sm.lay + g % 3) + 16 * threadIdx.x,
+                   reinterpret_cast<const char *>(dm.layers_g + g % dm.layers) + 16 * threadIdx.x);
+}
 
 // K1: RMSNorm + QKV + bias + RoPE + KV append (kernels_fused.go:47-73).
 // The QKV epilogue's inputs that do not depend on the token's activations
 // (bias, RoPE cos and sin of the position), and the attention norm's weights:
 // issued before the previous layer's down projection.
 __device__ __forceinline__ void qkv_prefetch(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm) {
-    const Layer &L = dm.layer[l];
+    const Layer &L = lay(sm, tk, l);
     const int cta = blockIdx.x, ncta = gridDim.x;
     const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, T = nq + nk + (L.v.rows >> 3);
     const int P = min(ncta, T);
     if (cta >= P) return;
     prefetch_norm(L.attn_norm, dm.embd, sm);
-    const int a = (int)((int64_t)T * cta / P), b = (int)((int64_t)T * (cta + 1) / P);
+    const int a = split_at(T, cta, P), b = split_at(T, cta + 1, P);
     const int hp = dm.head_dim >> 1;
     for (int i = threadIdx.x; i < (b - a) * 8; i += kConsThreads) {
         const int t = a + (i >> 3), r = i & 7;
@@ -894,7 +915,7 @@ __device__ __forceinline__ void qkv_prefetch(const DecParams &dm, int l, const T
 }
 
 __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
-    const Layer &L = dm.layer[l];
+    const Layer &L = lay(sm, tk, l);
     const int cta = blockIdx.x, ncta = gridDim.x;
     const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, T = nq + nk + (L.v.rows >> 3);
     const int P = min(ncta, T);
@@ -902,7 +923,7 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
     const int E = dm.embd, ev = l * 5 + PH_QKV;
     tk.tr.stamp(ev, 0);
     const uint32_t tag_in = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
-    const int a = (int)((int64_t)T * cta / P), b = (int)((int64_t)T * (cta + 1) / P);
+    const int a = split_at(T, cta, P), b = split_at(T, cta + 1, P);
     if (l == 0) {
         for (int e = threadIdx.x; e < E; e += kConsThreads) {
             const QMat &m = dm.embed;
@@ -970,35 +991,31 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
 // exp-weighted V sum (kernels_fused.go:82-146).  The chunk's cached K and V
 // rows do not depend on this token, so they are copied into shared memory
 // (cp.async) before the item waits for the token's q, k, v.  Each warp takes
-// a contiguous share of the positions, a lane per position for the scores
-// and a lane per HD/32 dimensions for the V sum, with its own max; the eight
-// warp partials are then combined.  With one chunk the item writes the
+// a share of the positions (a multiple of 8), a lane per position for the
+// scores and a lane per HD/32 dimensions for the V sum, with its own max; the
+// eight warp partials are then combined.  With one chunk the item writes the
 // head's output; otherwise the item holding the current position merges the
 // others' partials.  f32 arithmetic (the exp in double in cpu.go:321: within
 // 2 ulp), the merge of chunks in double.
 //
-// K/V rows sit in shared memory at a stride of HD floats with their 16-byte
-// groups permuted (group g of row p at g ^ (p & 15)): a quarter warp reading
-// the same group of 8 consecutive rows, or a warp reading one row, touches
-// each bank once.
-template <int HD>
-__device__ __forceinline__ int kv_swz(int p, int d) {
-    return p * HD + ((((d >> 2) ^ (p & 15))) << 2) + (d & 3);
-}
-
+// K rows sit at a stride of HD + 4 floats: a quarter warp reading the same
+// 16 bytes of 8 consecutive rows touches each bank once.  V rows are read a
+// row per warp instruction, at a stride of HD; the current position's V row
+// is polled into place, its K row into kc.
 template <int HD>
 __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, int nch, const DecSmem &sm) {
+    constexpr int KS = HD + 4;
     constexpr int V4 = HD / 4;
     constexpr int VD = HD / 32;  // V dimensions per lane
     const int grp = dm.heads / dm.kv_heads;
     const int h = item / nch, c = item % nch, kvh = h / grp;
     const int n = tk.pos + 1, C = dm.dec_chunk;
-    const Layer &L = dm.layer[l];
+    const Layer &L = lay(sm, tk, l);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
     const uint32_t otag = tag_of(tk.epoch, dm.layers, l, PH_ATT);
-    float *qh = sm.att, *kc = sm.att + HD, *vc = sm.att + 2 * HD;
+    float *qh = sm.att, *kc = sm.att + HD;
     float *wpart = sm.att + 3 * HD;  // [8 warps][HD + 4]: V sum, then max and sum of exp
-    float *ks = sm.kvs, *vs = sm.kvs + (size_t)C * HD;
+    float *ks = sm.kvs, *vs = sm.kvs + (size_t)C * KS;
     const int p0 = c * C, cnt = min(C, n - p0);
     const bool has_cur = p0 + cnt == n;
     const int nhist = has_cur ? cnt - 1 : cnt;
@@ -1008,68 +1025,70 @@ __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, i
     for (int i = threadIdx.x; i < nhist * V4; i += kConsThreads) {
         const int p = i / V4, d4 = i % V4;
         const size_t row = (size_t)(p0 + p) * dm.kvd + kvh * HD + d4 * 4;
-        cp_async16(ks + kv_swz<HD>(p, d4 * 4), L.kv + row);
-        cp_async16(vs + kv_swz<HD>(p, d4 * 4), L.kv + (size_t)dm.ctx * dm.kvd + row);
+        cp_async16(ks + p * KS + d4 * 4, L.kv + row);
+        cp_async16(vs + p * HD + d4 * 4, L.kv + (size_t)dm.ctx * dm.kvd + row);
     }
+    // V rows past the last position up to a multiple of 8 are read with weight 0: finite
+    const int cnt8 = (cnt + 7) & ~7;
+    for (int i = cnt * HD + threadIdx.x; i < cnt8 * HD; i += kConsThreads) vs[i] = 0.f;
     const int ncur = has_cur ? HD : 0;
     const Seg qkv[3] = {{dm.ll_q + h * HD, HD, tag, qh}, {dm.ll_k + kvh * HD, ncur, tag, kc},
-                        {dm.ll_v + kvh * HD, ncur, tag, vc}};
+                        {dm.ll_v + kvh * HD, ncur, tag, vs + nhist * HD}};
     const bool ok = poll_segs(qkv, dm.err);
     cp_async_wait_all();
     if (cons_or(!ok)) return false;
     tk.tr.stamp(ev, 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int per = (cnt + kCons - 1) / kCons;  // positions per warp (at most 32)
+    const int per = ((cnt + kCons - 1) / kCons + 7) & ~7;  // positions per warp: a multiple of 8, at most 32
     const int wp0 = warp * per, wcnt = max(0, min(per, cnt - wp0));
-    // scores: a lane per position (the current one's K row is kc, unpermuted)
+    // scores: a lane per position
     float sc = -FLT_MAX;
     if (lane < wcnt) {
         const int p = wp0 + lane;
-        const bool cur = p == nhist;
-        const float *kr = cur ? kc : ks + (size_t)p * HD;
-        const int sw = cur ? 0 : (p & 15);
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 4
+        const float *kr = p == nhist ? kc : ks + p * KS;
+        float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+#pragma unroll 8
         for (int g = 0; g < V4; ++g) {
-            const float4 k4 = *reinterpret_cast<const float4 *>(kr + ((g ^ sw) << 2));
+            const float4 k4 = *reinterpret_cast<const float4 *>(kr + 4 * g);
             const float4 q4 = *reinterpret_cast<const float4 *>(qh + 4 * g);
-            a0 = fmaf(q4.x, k4.x, a0);
-            a1 = fmaf(q4.y, k4.y, a1);
-            a2 = fmaf(q4.z, k4.z, a2);
-            a3 = fmaf(q4.w, k4.w, a3);
+            a01 = __ffma2_rn(make_float2(q4.x, q4.y), make_float2(k4.x, k4.y), a01);
+            a23 = __ffma2_rn(make_float2(q4.z, q4.w), make_float2(k4.z, k4.w), a23);
         }
-        sc = __fmul_rn((a0 + a1) + (a2 + a3), dm.scale);
+        sc = __fmul_rn((a01.x + a01.y) + (a23.x + a23.y), dm.scale);
     }
     float mx = sc;
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
     const float e = lane < wcnt ? expf(__fsub_rn(sc, mx)) : 0.f;  // cpu.go:321
-    float ls = e;
+    // the V sum, 8 positions at a time, and the sum of exp alongside
+    float2 ov[VD / 2];
 #pragma unroll
-    for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(kFull, ls, o);
-    float ov[VD];
+    for (int k = 0; k < VD / 2; ++k) ov[k] = make_float2(0.f, 0.f);
+    float ls = 0.f;
+    for (int j0 = 0; j0 < wcnt; j0 += 8) {
+        const float *vb = vs + (wp0 + j0) * HD + VD * lane;
+        float w[8];
+        float2 v[8][VD / 2];
 #pragma unroll
-    for (int k = 0; k < VD; ++k) ov[k] = 0.f;
-    for (int j = 0; j < wcnt; ++j) {
-        const float w = __shfl_sync(kFull, e, j);
-        const int p = wp0 + j;
-        const bool cur = p == nhist;
-        const float *vr = cur ? vc + VD * lane : vs + kv_swz<HD>(p, VD * lane);
-        if constexpr (VD == 2) {
-            const float2 v2 = *reinterpret_cast<const float2 *>(vr);
-            ov[0] = fmaf(w, v2.x, ov[0]);
-            ov[1] = fmaf(w, v2.y, ov[1]);
-        } else {
-            const float4 v4 = *reinterpret_cast<const float4 *>(vr);
-            ov[0] = fmaf(w, v4.x, ov[0]);
-            ov[1] = fmaf(w, v4.y, ov[1]);
-            ov[2] = fmaf(w, v4.z, ov[2]);
-            ov[3] = fmaf(w, v4.w, ov[3]);
+        for (int k = 0; k < 8; ++k) {
+            w[k] = __shfl_sync(kFull, e, j0 + k);
+            if constexpr (VD == 2) {
+                v[k][0] = *reinterpret_cast<const float2 *>(vb + k * HD);
+            } else {
+                const float4 t = *reinterpret_cast<const float4 *>(vb + k * HD);
+                v[k][0] = make_float2(t.x, t.y), v[k][1] = make_float2(t.z, t.w);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            ls += w[k];
+#pragma unroll
+            for (int i = 0; i < VD / 2; ++i) ov[i] = __ffma2_rn(make_float2(w[k], w[k]), v[k][i], ov[i]);
         }
     }
     float *wp = wpart + warp * (HD + 4);
 #pragma unroll
-    for (int k = 0; k < VD; ++k) wp[VD * lane + k] = ov[k];
+    for (int k = 0; k < VD / 2; ++k) *reinterpret_cast<float2 *>(wp + VD * lane + 2 * k) = ov[k];
     if (lane == 0) wp[HD] = mx, wp[HD + 1] = ls;
     cons_sync();
     // the warps' partials combined: thread d < HD sums dimension d
@@ -1138,7 +1157,7 @@ __device__ bool ph_attn(const DecParams &dm, int l, const Tok &tk, int item, int
 
 // K3: x += Wo att (cpu.go:336-339).
 __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
-    const Layer &L = dm.layer[l];
+    const Layer &L = lay(sm, tk, l);
     const Share s = share(L.o, blockIdx.x, gridDim.x, rg.slot_bytes);
     if (s.b <= s.a) return true;
     const uint32_t tin = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
@@ -1165,7 +1184,7 @@ __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &s
 
 // K4: RMSNorm + gate/up + SwiGLU (cpu.go:340-346).
 __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
-    const Layer &L = dm.layer[l];
+    const Layer &L = lay(sm, tk, l);
     const Share sg = share(L.gate, blockIdx.x, gridDim.x, rg.slot_bytes);
     const Share su = share(L.up, blockIdx.x, gridDim.x, rg.slot_bytes);
     if (sg.b <= sg.a) return true;
@@ -1216,7 +1235,7 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
 
 // K5: x += Wdown act (cpu.go:347-350).
 __device__ bool ph_down(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
-    const Layer &L = dm.layer[l];
+    const Layer &L = lay(sm, tk, l);
     const Share s = share(L.down, blockIdx.x, gridDim.x, rg.slot_bytes);
     if (s.b <= s.a) return true;
     const int F = dm.ff;
@@ -1389,7 +1408,10 @@ __device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *
     tk.pos = (int)__ldcg(dm.state), tk.step = (int)__ldcg(dm.state + 1);
     tk.tok = __ldcg(dm.tokens + tk.step);
     tk.epoch = __ldcg(dm.ll_epoch);
+    fetch_layer(dm, sm, 0);
+    fetch_layer(dm, sm, 1);
     for (int i = 0; i < ntok; ++i) {
+        tk.g0 = i * dm.layers;
         if (tk.pos >= dm.ctx) {
             if (threadIdx.x == 0) atomicExch(dm.err, DEV_CONTEXT_FULL);
             return;
@@ -1409,14 +1431,21 @@ __device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *
                 ll_put(dm.ll_x + e, v, tag_of(tk.epoch, dm.layers, -1, PH_DOWN));
             }
         }
+        cp_async_wait_all();  // layers 0 and 1 of the token
+        cons_sync();
         qkv_prefetch(dm, 0, tk, sm);
         for (int l = 0; l < dm.layers; ++l) {
+            if (l > 0) {  // layer l + 1's descriptor (and this layer's prefetches), then layer l + 2's copy
+                cp_async_wait_all();
+                cons_sync();
+            }
+            fetch_layer(dm, sm, tk.g0 + l + 2);
             if (!ph_qkv(dm, l, tk, sm, rg)) return;
             // attention items from the last CTA down: those have no QKV, output
             // or down rows, so they copy the K/V history well before q, k, v arrive
             for (int item = gridDim.x - 1 - blockIdx.x; item < dm.heads * nch; item += gridDim.x)
                 if (!ph_attn(dm, l, tk, item, nch, sm)) return;
-            prefetch_norm(dm.layer[l].ffn_norm, dm.embd, sm);
+            prefetch_norm(lay(sm, tk, l).ffn_norm, dm.embd, sm);
             if (!ph_o(dm, l, tk, sm, rg)) return;
             if (!ph_gu(dm, l, tk, sm, rg)) return;
             if (l + 1 < dm.layers) qkv_prefetch(dm, l + 1, tk, sm);
@@ -1451,6 +1480,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         sm.full = reinterpret_cast<uint64_t *>(dsm + lo.full);
         sm.feed = reinterpret_cast<Feed *>(dsm + lo.feed);
         sm.plan = reinterpret_cast<FeedUnit *>(dsm + lo.plan);
+        sm.lay = reinterpret_cast<Layer *>(dsm + lo.lay);
         sm.xv = reinterpret_cast<float *>(dsm + lo.xv);
         sm.xq8 = reinterpret_cast<float *>(dsm + lo.xq8);
         sm.xs = reinterpret_cast<float *>(dsm + lo.xs);
@@ -1477,6 +1507,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         for (int i = 0; i < nslots; ++i) feed_issue(sm, nslots, slot_bytes);
     Ring rg{nslots, slot_bytes, 0u};
     decode_tokens(dm, bar, ntok, sm, rg);
+    cp_async_wait_all();  // descriptor copies of layers past the launch's last
     if (threadIdx.x == kFeeder) feed_drain(sm, nslots, rg.u);
 }
 

@@ -41,7 +41,7 @@ __host__ __device__ inline int tile_bytes_of(int type, int nb) {
     return per_block * nb;
 }
 
-struct Layer {
+struct alignas(16) Layer {  // 16-byte aligned: the decode kernel copies it in 16-byte pieces
     QMat q, k, v;  // q and k rows in adjacent-pair RoPE order (NEOX rows permuted at load)
     QMat o, gate, up, down;
     const float *attn_norm = nullptr, *ffn_norm = nullptr;
@@ -110,6 +110,7 @@ struct ModelHeader {
     int dec_gate_rows;   // gate rows of the largest gate/up share of a CTA
     int dec_qkv_rows;    // rows of the largest QKV share of a CTA
     int dec_chunk;       // positions per attention item (a multiple of 32, 64..256)
+    const Layer *layers_g;  // the layers' descriptors in device memory (the decode kernel stages them in shared memory)
     // each CTA's units of one token, in consumption order (plan[cta * kMaxFeedPlan + j],
     // feed_count[cta] of them; feed_max the largest count), built once per model
     const FeedUnit *feed_plan;
@@ -142,7 +143,7 @@ static_assert(sizeof(DecParams) < 32000, "kernel parameters are limited to 32 KB
 
 // Shared-memory layout of the persistent decode kernel (byte offsets).
 struct DecLayout {
-    size_t ring, full, feed, plan, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, nrm, total;
+    size_t ring, full, feed, plan, lay, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, nrm, total;
 };
 
 __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int embd, int ff, int head_dim, int heads,
@@ -154,6 +155,8 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     l.full = p, p += 8 * (size_t)nslots;
     l.feed = p, p += 32;
     l.plan = p, p += sizeof(FeedUnit) * (size_t)plan_units;
+    p = (p + 15) / 16 * 16;
+    l.lay = p, p += 3 * sizeof(Layer);
     p = (p + 127) / 128 * 128;
     l.xv = p, p += vec;
     l.xq8 = p, p += vec;
@@ -161,10 +164,11 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     l.part = p, p += 8 * 64;
     l.rows = p, p += 4 * 256;
     l.gate = p, p += 4 * (size_t)gate_rows;
-    // an attention item's history K and V rows [2][dec_chunk][head_dim] share
-    // the bytes of the matrix phases' vectors above (no phase uses both)
+    // an attention item's history K rows [dec_chunk][head_dim + 4] and V rows
+    // [dec_chunk][head_dim] share the bytes of the matrix phases' vectors
+    // above (no phase uses both)
     l.kvs = l.xv;
-    const size_t kv_end = l.kvs + 4 * (size_t)2 * dec_chunk * head_dim;
+    const size_t kv_end = l.kvs + 4 * (size_t)dec_chunk * (2 * head_dim + 4);
     p = p > kv_end ? p : kv_end;
     p = (p + 15) / 16 * 16;
     l.red = p, p += 4 * 64;

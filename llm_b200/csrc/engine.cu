@@ -430,6 +430,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     if (!(plan_count = m.alloc<int>((size_t)m.persistent_ctas * 4, err))) return err;
     d.feed_plan = plan, d.feed_count = plan_count;
     if (!(m.dm = m.alloc<DevModel>(sizeof(DevModel), err))) return err;
+    d.layers_g = m.dm->layer;  // the device address of the array (nothing is read here)
     CUDA_TRY(cudaMemcpyAsync(m.dm, &d, sizeof(DevModel), cudaMemcpyHostToDevice, m.st));
     m.dp = std::make_unique<DecParams>();
     static_cast<ModelHeader &>(*m.dp) = static_cast<const ModelHeader &>(d);
