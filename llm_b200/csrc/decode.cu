@@ -272,6 +272,19 @@ struct Share {
 // long dependent sequence that sat at the head of every phase.
 __device__ __forceinline__ int split_at(int T, int i, int P) { return (int)((unsigned)T * (unsigned)i / (unsigned)P); }
 
+// The CTA's share of each kind of matrix, computed once per launch: the rows
+// of a kind are the same in every layer, and `per` depends only on the
+// format.  (Integer divisions are long dependent sequences; at the head of a
+// phase they delayed its first poll.)
+enum { SK_QKV = 0, SK_O, SK_GU, SK_DOWN, SK_HEAD, SK_N };
+struct ShareTab {
+    int a[SK_N], b[SK_N];  // tiles [a, b) of the kind (QKV: of q, k, v in turn)
+    int per[SK_N][3];      // tiles per unit by format: Q4_0, Q4_1, Q8_0
+};
+static_assert(sizeof(ShareTab) <= 128, "the shared-memory layout reserves 128 bytes");
+
+__device__ __forceinline__ int fmt_ix(int type) { return type == 8 ? 2 : type == 3 ? 1 : 0; }
+
 __device__ __forceinline__ Share share(const QMat &m, int cta, int ncta, int slot_bytes) {
     const int T = m.rows >> 3;
     const int P = min(ncta, T);
@@ -292,6 +305,7 @@ struct DecSmem {
     uint64_t *full;          // ring mbarriers (one per slot)
     struct Feed *feed;       // the feeder thread's cursor
     FeedUnit *plan;          // the CTA's units of one token
+    ShareTab *st;            // the CTA's shares (computed at launch)
     Layer *lay;              // descriptors of the current and the next two layers (buffer g % 3, g = layers so far)
     uint8_t *ring;           // nslots * slot_bytes
     float *xv;               // activation vector, paired layout for Q4 / plain for Q8 (max(E,F) floats)
@@ -307,6 +321,10 @@ struct DecSmem {
     float *kvs;              // an attention item's history K rows, then V rows (aliases xv..gate)
     float *nrm;              // the next norm's weights (embd floats)
 };
+
+__device__ __forceinline__ Share share_of(const DecSmem &sm, int kind, const QMat &m) {
+    return Share{sm.st->a[kind], sm.st->b[kind], sm.st->per[kind][fmt_ix(m.type)]};
+}
 
 // --------------------------------------------------------- dot products --
 // The activation vector is staged block by block with a stride of kXB floats
@@ -467,7 +485,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // aligned), issued at the start of the phase before the one that uses them:
 // the copies complete while that phase runs, off the path from the input's
 // arrival to the first dot product.  norm_fold waits for them.
+// cp.async copies complete in no fixed order, so the thread's earlier copies
+// (an earlier norm's, into the same bytes) are waited for first; normally
+// they are long done.
 __device__ __forceinline__ void prefetch_norm(const float *w, int E, const DecSmem &sm) {
+    cp_async_wait_all();
     for (int i = threadIdx.x; 4 * i < E; i += kConsThreads) cp_async16(sm.nrm + 4 * i, w + 4 * i);
 }
 
@@ -624,7 +646,13 @@ __device__ __forceinline__ float norm_scale(const DecParams &dm, const DecSmem &
 
 struct Ring {
     int nslots, slot_bytes;
-    unsigned u;  // units consumed so far
+    unsigned u;   // units consumed so far
+    int sl;       // u % nslots
+    unsigned ph;  // (u / nslots) & 1: the parity of the slot's fill
+    __device__ __forceinline__ void next() {
+        ++u;
+        if (++sl == nslots) sl = 0, ph ^= 1u;
+    }
 };
 
 // The shared-memory views the tile pipeline needs (by value, so the
@@ -640,15 +668,14 @@ struct UnitCtx {
 // takes whole tiles, otherwise every tile's blocks are split across the
 // warps, whose partials meet through shared memory and three shuffles, in a
 // fixed order.
-__device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const UnitCtx &c, const int nslots,
-                                             const int slot_bytes, const unsigned u, int *err) {
+__device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const UnitCtx &c, const int sl,
+                                             const unsigned ph, const int slot_bytes, int *err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint64_t w0 = threadIdx.x == 0 ? clock64() : 0;
-    const int sl = u % nslots;
     bool ok = true;
-    if (!mbar_try_wait(c.full + sl, (u / nslots) & 1)) {
+    if (!mbar_try_wait(c.full + sl, ph)) {
         const uint64_t t0 = gtimer();
-        while (!mbar_try_wait(c.full + sl, (u / nslots) & 1)) {
+        while (!mbar_try_wait(c.full + sl, ph)) {
             if (read_err(err)) {
                 ok = false;
                 break;
@@ -678,11 +705,12 @@ __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const U
         const float a = dot_row(m.type, slot, m.nb, warp, sm, lane);
         if (lane == 0) c.rows[warp] = a;
     } else {
-        const int parts = kCons / k;
-        const int tile = warp / parts, part = warp % parts;
+        const int lg = k == 2 ? 2 : k <= 4 ? 1 : 0;  // parts = kCons / k = 1 << lg (k in 2..7), by shifts
+        const int parts = 1 << lg;
+        const int tile = warp >> lg, part = warp & (parts - 1);
         float a = 0.f;
         if (tile < k) {
-            const int b0 = m.nb * part / parts, b1 = m.nb * (part + 1) / parts;
+            const int b0 = (m.nb * part) >> lg, b1 = (m.nb * (part + 1)) >> lg;
             a = dot_tile(m.type, slot + (size_t)tile * m.tile_bytes, m.nb, sm, b0, b1, lane);
         }
         __syncwarp();
@@ -699,7 +727,7 @@ __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const U
             if (parts >= 2) v += __shfl_xor_sync(kFull, v, 1);
             if (parts >= 4) v += __shfl_xor_sync(kFull, v, 2);
             if (parts >= 8) v += __shfl_xor_sync(kFull, v, 4);
-            if (w % parts == 0 && w / parts < k) c.rows[(w / parts) * 8 + (threadIdx.x >> 3)] = v;
+            if ((w & (parts - 1)) == 0 && (w >> lg) < k) c.rows[(w >> lg) * 8 + (threadIdx.x >> 3)] = v;
         }
     }
     cons_sync();
@@ -711,8 +739,8 @@ __device__ __forceinline__ void feed_issue(const DecSmem &sm, int nslots, int sl
 // One unit: its rows into sm.rows; then the feeder refills the slot it used.
 __device__ __forceinline__ bool unit_rows(const DecParams &dm, const QMat &m, int k, const DecSmem &sm, Ring &rg) {
     const UnitCtx c{sm.full, sm.ring, sm.xv, sm.xq8, reinterpret_cast<float *>(sm.part), sm.rows};
-    const bool ok = unit_rows_nl(m, k, c, rg.nslots, rg.slot_bytes, rg.u, dm.err);
-    rg.u++;
+    const bool ok = unit_rows_nl(m, k, c, rg.sl, rg.ph, rg.slot_bytes, dm.err);
+    rg.next();
     if (ok && threadIdx.x == kFeeder) feed_issue(sm, rg.nslots, rg.slot_bytes);
     return ok;
 }
@@ -751,7 +779,9 @@ struct Feed {
     unsigned issued;  // units issued
     int j, n;         // decoding: the next plan entry, entries per token
     unsigned total;   // units of the launch
+    int sl;           // the slot of the next issue (issued % nslots)
 };
+static_assert(sizeof(Feed) <= 64, "the shared-memory layout reserves 64 bytes");
 
 __device__ __forceinline__ bool share_unit(const QMat &m, const Share &s, int &ft, const uint8_t *&src, unsigned &n) {
     const int t = s.a + ft;
@@ -822,7 +852,8 @@ __device__ __forceinline__ void feed_issue(const DecSmem &sm, int nslots, int sl
     if (f.issued >= f.total) return;
     const FeedUnit e = sm.plan[f.j];
     f.j = f.j + 1 == f.n ? 0 : f.j + 1;
-    const int slot = f.issued % (unsigned)nslots;
+    const int slot = f.sl;
+    f.sl = f.sl + 1 == nslots ? 0 : f.sl + 1;
     uint8_t *dst = sm.ring + (size_t)slot * slot_bytes;
     // the slot's previous contents were read through the generic proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -892,12 +923,10 @@ __device__ __forceinline__ void fetch_layer(const DecParams &dm, const DecSmem &
 // issued before the previous layer's down projection.
 __device__ __forceinline__ void qkv_prefetch(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm) {
     const Layer &L = lay(sm, tk, l);
-    const int cta = blockIdx.x, ncta = gridDim.x;
-    const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, T = nq + nk + (L.v.rows >> 3);
-    const int P = min(ncta, T);
-    if (cta >= P) return;
+    const int a = sm.st->a[SK_QKV], b = sm.st->b[SK_QKV];
+    if (b <= a) return;
+    const int nq = L.q.rows >> 3, nk = L.k.rows >> 3;
     prefetch_norm(L.attn_norm, dm.embd, sm);
-    const int a = split_at(T, cta, P), b = split_at(T, cta + 1, P);
     const int hp = dm.head_dim >> 1;
     for (int i = threadIdx.x; i < (b - a) * 8; i += kConsThreads) {
         const int t = a + (i >> 3), r = i & 7;
@@ -908,7 +937,7 @@ __device__ __forceinline__ void qkv_prefetch(const DecParams &dm, int l, const T
         else sm.pre[4 * i] = 0.f;
         if (seg < 2)
             cp_async8(sm.pre + 4 * i + 2, reinterpret_cast<const float2 *>(dm.rope_cs) + (size_t)tk.pos * hp +
-                                              ((row % dm.head_dim) >> 1));
+                                              ((row & (dm.head_dim - 1)) >> 1));  // head_dim: 64 or 128
         else
             sm.pre[4 * i + 2] = 1.f, sm.pre[4 * i + 3] = 0.f;
     }
@@ -916,14 +945,12 @@ __device__ __forceinline__ void qkv_prefetch(const DecParams &dm, int l, const T
 
 __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Layer &L = lay(sm, tk, l);
-    const int cta = blockIdx.x, ncta = gridDim.x;
-    const int nq = L.q.rows >> 3, nk = L.k.rows >> 3, T = nq + nk + (L.v.rows >> 3);
-    const int P = min(ncta, T);
-    if (cta >= P) return true;
+    const int a = sm.st->a[SK_QKV], b = sm.st->b[SK_QKV];
+    if (b <= a) return true;
+    const int nq = L.q.rows >> 3, nk = L.k.rows >> 3;
     const int E = dm.embd, ev = l * 5 + PH_QKV;
     tk.tr.stamp(ev, 0);
     const uint32_t tag_in = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
-    const int a = split_at(T, cta, P), b = split_at(T, cta + 1, P);
     if (l == 0) {
         for (int e = threadIdx.x; e < E; e += kConsThreads) {
             const QMat &m = dm.embed;
@@ -1158,7 +1185,7 @@ __device__ bool ph_attn(const DecParams &dm, int l, const Tok &tk, int item, int
 // K3: x += Wo att (cpu.go:336-339).
 __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Layer &L = lay(sm, tk, l);
-    const Share s = share(L.o, blockIdx.x, gridDim.x, rg.slot_bytes);
+    const Share s = share_of(sm, SK_O, L.o);
     if (s.b <= s.a) return true;
     const uint32_t tin = tag_of(tk.epoch, dm.layers, l - 1, PH_DOWN);
     const int ev = l * 5 + PH_O;
@@ -1185,8 +1212,8 @@ __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &s
 // K4: RMSNorm + gate/up + SwiGLU (cpu.go:340-346).
 __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Layer &L = lay(sm, tk, l);
-    const Share sg = share(L.gate, blockIdx.x, gridDim.x, rg.slot_bytes);
-    const Share su = share(L.up, blockIdx.x, gridDim.x, rg.slot_bytes);
+    const Share sg = share_of(sm, SK_GU, L.gate);
+    const Share su = share_of(sm, SK_GU, L.up);
     if (sg.b <= sg.a) return true;
     const int E = dm.embd, ev = l * 5 + PH_GU;
     tk.tr.stamp(ev, 0);
@@ -1236,7 +1263,7 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
 // K5: x += Wdown act (cpu.go:347-350).
 __device__ bool ph_down(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Layer &L = lay(sm, tk, l);
-    const Share s = share(L.down, blockIdx.x, gridDim.x, rg.slot_bytes);
+    const Share s = share_of(sm, SK_DOWN, L.down);
     if (s.b <= s.a) return true;
     const int F = dm.ff;
     const uint32_t tact = tag_of(tk.epoch, dm.layers, l, PH_GU), tin = tag_of(tk.epoch, dm.layers, l, PH_O);
@@ -1271,11 +1298,11 @@ __device__ __forceinline__ bool head_unit(const DecParams &dm, int k, int t0, fl
                                           float &bv, int &bi) {
     const QMat &m = dm.head;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int sl = rg.u % rg.nslots;
+    const int sl = rg.sl;
     bool ok = true;
-    if (!mbar_try_wait(sm.full + sl, (rg.u / rg.nslots) & 1)) {
+    if (!mbar_try_wait(sm.full + sl, rg.ph)) {
         const uint64_t t0w = gtimer();
-        while (!mbar_try_wait(sm.full + sl, (rg.u / rg.nslots) & 1)) {
+        while (!mbar_try_wait(sm.full + sl, rg.ph)) {
             if (read_err(dm.err)) {
                 ok = false;
                 break;
@@ -1305,11 +1332,12 @@ __device__ __forceinline__ bool head_unit(const DecParams &dm, int k, int t0, fl
             if ((lane & 3) == 0) finish(i, lane >> 2, a);
         }
     } else {
-        const int parts = kCons / k;
-        const int tile = warp / parts, part = warp % parts;
+        const int lg = k == 2 ? 2 : k <= 4 ? 1 : 0;  // parts = kCons / k = 1 << lg (k in 2..7), by shifts
+        const int parts = 1 << lg;
+        const int tile = warp >> lg, part = warp & (parts - 1);
         float a = 0.f;
         if (tile < k) {
-            const int b0 = m.nb * part / parts, b1 = m.nb * (part + 1) / parts;
+            const int b0 = (m.nb * part) >> lg, b1 = (m.nb * (part + 1)) >> lg;
             a = dot_tile(m.type, slot + (size_t)tile * m.tile_bytes, m.nb, sm, b0, b1, lane);
         }
         a += __shfl_xor_sync(kFull, a, 1);
@@ -1323,17 +1351,17 @@ __device__ __forceinline__ bool head_unit(const DecParams &dm, int k, int t0, fl
             if (parts >= 2) v += __shfl_xor_sync(kFull, v, 1);
             if (parts >= 4) v += __shfl_xor_sync(kFull, v, 2);
             if (parts >= 8) v += __shfl_xor_sync(kFull, v, 4);
-            if (w % parts == 0 && w / parts < k) finish(w / parts, threadIdx.x >> 3, v);
+            if ((w & (parts - 1)) == 0 && (w >> lg) < k) finish(w >> lg, threadIdx.x >> 3, v);
         }
     }
     cons_sync();  // the slot (and the shared partials) are free
-    rg.u++;
+    rg.next();
     if (threadIdx.x == kFeeder) feed_issue(sm, rg.nslots, rg.slot_bytes);
     return true;
 }
 
 __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, Ring &rg) {
-    const Share s = share(dm.head, blockIdx.x, gridDim.x, rg.slot_bytes);
+    const Share s = share_of(sm, SK_HEAD, dm.head);
     float bv = -FLT_MAX;
     int bi = 0x7fffffff;
     const int ev = dm.layers * 5;
@@ -1445,7 +1473,7 @@ __device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *
             // or down rows, so they copy the K/V history well before q, k, v arrive
             for (int item = gridDim.x - 1 - blockIdx.x; item < dm.heads * nch; item += gridDim.x)
                 if (!ph_attn(dm, l, tk, item, nch, sm)) return;
-            prefetch_norm(lay(sm, tk, l).ffn_norm, dm.embd, sm);
+            if (sm.st->b[SK_GU] > sm.st->a[SK_GU]) prefetch_norm(lay(sm, tk, l).ffn_norm, dm.embd, sm);
             if (!ph_o(dm, l, tk, sm, rg)) return;
             if (!ph_gu(dm, l, tk, sm, rg)) return;
             if (l + 1 < dm.layers) qkv_prefetch(dm, l + 1, tk, sm);
@@ -1481,6 +1509,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         sm.feed = reinterpret_cast<Feed *>(dsm + lo.feed);
         sm.plan = reinterpret_cast<FeedUnit *>(dsm + lo.plan);
         sm.lay = reinterpret_cast<Layer *>(dsm + lo.lay);
+        sm.st = reinterpret_cast<ShareTab *>(dsm + lo.shares);
         sm.xv = reinterpret_cast<float *>(dsm + lo.xv);
         sm.xq8 = reinterpret_cast<float *>(dsm + lo.xq8);
         sm.xs = reinterpret_cast<float *>(dsm + lo.xs);
@@ -1494,18 +1523,33 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         sm.kvs = reinterpret_cast<float *>(dsm + lo.kvs);
         sm.nrm = reinterpret_cast<float *>(dsm + lo.nrm);
     }
+    if (threadIdx.x < 4 * SK_N) {  // the share table: a thread per entry
+        const Layer &L0 = dm.layer[0];
+        const int kind = threadIdx.x % SK_N, what = threadIdx.x / SK_N;
+        const QMat &m = kind == SK_QKV ? L0.q : kind == SK_O ? L0.o : kind == SK_GU ? L0.gate
+                                             : kind == SK_DOWN ? L0.down : dm.head;
+        if (what == 0) {
+            const int T = kind == SK_QKV ? (L0.q.rows + L0.k.rows + L0.v.rows) >> 3 : m.rows >> 3;
+            const int P = min((int)gridDim.x, T), cta = blockIdx.x;
+            sm.st->a[kind] = cta < P ? split_at(T, cta, P) : 0;
+            sm.st->b[kind] = cta < P ? split_at(T, cta + 1, P) : 0;
+        } else {
+            const int type = what == 1 ? 2 : what == 2 ? 3 : 8;  // formats in fmt_ix order
+            sm.st->per[kind][what - 1] = max(1, min(kConsThreads / 8, slot_bytes / tile_bytes_of(type, m.nb)));
+        }
+    }
     const int nplan = __ldg(dm.feed_count + blockIdx.x);
     for (int j = threadIdx.x; j < nplan; j += kConsThreads)
         sm.plan[j] = dm.feed_plan[(size_t)blockIdx.x * kMaxFeedPlan + j];
     if (threadIdx.x == 0) {
         for (int i = 0; i < nslots; ++i) mbar_init(sm.full + i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        *sm.feed = Feed{0, 0, 0, 0, 0u, 0, nplan, (unsigned)(ntok * nplan)};
+        *sm.feed = Feed{0, 0, 0, 0, 0u, 0, nplan, (unsigned)(ntok * nplan), 0};
     }
     __syncthreads();
     if (threadIdx.x == kFeeder)
         for (int i = 0; i < nslots; ++i) feed_issue(sm, nslots, slot_bytes);
-    Ring rg{nslots, slot_bytes, 0u};
+    Ring rg{nslots, slot_bytes, 0u, 0, 0u};
     decode_tokens(dm, bar, ntok, sm, rg);
     cp_async_wait_all();  // descriptor copies of layers past the launch's last
     if (threadIdx.x == kFeeder) feed_drain(sm, nslots, rg.u);

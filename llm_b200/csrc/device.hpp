@@ -143,7 +143,7 @@ static_assert(sizeof(DecParams) < 32000, "kernel parameters are limited to 32 KB
 
 // Shared-memory layout of the persistent decode kernel (byte offsets).
 struct DecLayout {
-    size_t ring, full, feed, plan, lay, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, nrm, total;
+    size_t ring, full, feed, plan, lay, shares, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, nrm, total;
 };
 
 __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int embd, int ff, int head_dim, int heads,
@@ -153,10 +153,11 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     size_t p = 0;
     l.ring = p, p += (size_t)nslots * slot_bytes;
     l.full = p, p += 8 * (size_t)nslots;
-    l.feed = p, p += 32;
+    l.feed = p, p += 64;
     l.plan = p, p += sizeof(FeedUnit) * (size_t)plan_units;
     p = (p + 15) / 16 * 16;
     l.lay = p, p += 3 * sizeof(Layer);
+    l.shares = p, p += 128;  // ShareTab (decode.cu)
     p = (p + 127) / 128 * 128;
     l.xv = p, p += vec;
     l.xq8 = p, p += vec;

@@ -414,6 +414,15 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
         const int To = E / 8, Po = std::min(m.persistent_ctas, To);
         d.dec_gate_rows = std::max(d.dec_gate_rows, (To + Po - 1) / Po * 8);
         if (E > 1024) return {LLMB_ERR_CONFIG, "llm: the decode kernel supports embedding sizes up to 1024"};
+        // the kernel splits each kind of matrix once per launch, from layer 0's shapes
+        for (int l = 1; l < c.layers; l++) {
+            const Layer &a = d.layer[0], &b = d.layer[l];
+            const QMat *ma[] = {&a.q, &a.k, &a.v, &a.o, &a.gate, &a.up, &a.down};
+            const QMat *mb[] = {&b.q, &b.k, &b.v, &b.o, &b.gate, &b.up, &b.down};
+            for (int i = 0; i < 7; i++)
+                if (ma[i]->rows != mb[i]->rows || ma[i]->nb != mb[i]->nb)
+                    return {LLMB_ERR_CONFIG, "llm: the decode kernel needs every layer to have layer 0's shapes"};
+        }
         if (c.head_dim != 64 && c.head_dim != 128)
             return {LLMB_ERR_CONFIG, "llm: the decode kernel supports head sizes 64 and 128"};
         m.dec = decode_config(s, max_tile, d.head.tile_bytes, d.dec_gate_rows, d.dec_qkv_rows, 0,
