@@ -623,22 +623,25 @@ __device__ __noinline__ bool poll_stage_res(const uint64_t *src0, int n0, uint32
 }
 
 // The warps' partial sums of squares into red[32..39] (norm_scale reads them).
-__device__ __forceinline__ void norm_sums(float ss, const DecSmem &sm) {
+// (No barrier: the next consumer barrier publishes them.)
+__device__ __forceinline__ void norm_partial(float ss, const DecSmem &sm) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
     if ((threadIdx.x & 31) == 0) sm.red[32 + (threadIdx.x >> 5)] = ss;
-    cons_sync();
 }
 
-// 1 / sqrt(mean of squares + eps), from norm_fold's partials (fixed order):
-// cpu.go:94 rounds 1/sqrt computed in double to float; rsqrt in double is
-// within an ulp of that double, far below float's rounding.
+// 1 / sqrt(mean of squares + eps), from the warps' partials (fixed order):
+// cpu.go:94 rounds 1/sqrt computed in double to float.  Here a float seed
+// (rsqrtf, within 2 ulp) and one Newton step in double (error ~1e-13
+// relative), rounded to float: the same float but where the exact value is
+// within ~1e-13 of a rounding boundary.  Much shorter than a double rsqrt.
 __device__ __forceinline__ float norm_scale(const DecParams &dm, const DecSmem &sm) {
     float ss = 0.f;
 #pragma unroll
     for (int w = 0; w < kCons; ++w) ss += sm.red[32 + w];
     const float t = __fadd_rn(__fdiv_rn(ss, (float)dm.embd), dm.eps);
-    return (float)rsqrt((double)t);
+    const double y = (double)rsqrtf(t), td = (double)t;
+    return (float)(y * fma(-0.5 * td, y * y, 1.5));
 }
 
 // ------------------------------------------------------------- consume --
@@ -668,27 +671,32 @@ struct UnitCtx {
 // takes whole tiles, otherwise every tile's blocks are split across the
 // warps, whose partials meet through shared memory and three shuffles, in a
 // fixed order.
-__device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const UnitCtx &c, const int sl,
-                                             const unsigned ph, const int slot_bytes, int *err) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t w0 = threadIdx.x == 0 ? clock64() : 0;
+// This thread's wait for a ring slot's fill (false: timed out or a device
+// error; the caller's consumer barrier makes the outcome uniform).
+__device__ __forceinline__ bool slot_wait(uint64_t *full, int sl, unsigned ph, int *err) {
+    if (mbar_try_wait(full + sl, ph)) return true;
+    const uint64_t w0 = clock64(), t0 = gtimer();
     bool ok = true;
-    if (!mbar_try_wait(c.full + sl, ph)) {
-        const uint64_t t0 = gtimer();
-        while (!mbar_try_wait(c.full + sl, ph)) {
-            if (read_err(err)) {
-                ok = false;
-                break;
-            }
-            if (gtimer() - t0 > kWaitNs) {
-                atomicExch(err, DEV_RING_TIMEOUT);
-                ok = false;
-                break;
-            }
+    while (!mbar_try_wait(full + sl, ph)) {
+        if (read_err(err)) {
+            ok = false;
+            break;
+        }
+        if (gtimer() - t0 > kWaitNs) {
+            atomicExch(err, DEV_RING_TIMEOUT);
+            ok = false;
+            break;
         }
     }
-    if (cons_or(!ok)) return false;
     if (threadIdx.x == 0) s_ring_wait += clock64() - w0;
+    return ok;
+}
+
+// waited: the caller has waited for the slot and passed a consumer barrier since.
+__device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const UnitCtx &c, const int sl,
+                                             const unsigned ph, const int slot_bytes, int *err, bool waited) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (!waited && cons_or(!slot_wait(c.full, sl, ph, err))) return false;
     const uint8_t *slot = c.ring + (size_t)sl * slot_bytes;
     DecSmem sm;
     sm.xv = c.xv, sm.xq8 = c.xq8;
@@ -737,9 +745,10 @@ __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const U
 __device__ __forceinline__ void feed_issue(const DecSmem &sm, int nslots, int slot_bytes);
 
 // One unit: its rows into sm.rows; then the feeder refills the slot it used.
-__device__ __forceinline__ bool unit_rows(const DecParams &dm, const QMat &m, int k, const DecSmem &sm, Ring &rg) {
+__device__ __forceinline__ bool unit_rows(const DecParams &dm, const QMat &m, int k, const DecSmem &sm, Ring &rg,
+                                          bool waited = false) {
     const UnitCtx c{sm.full, sm.ring, sm.xv, sm.xq8, reinterpret_cast<float *>(sm.part), sm.rows};
-    const bool ok = unit_rows_nl(m, k, c, rg.sl, rg.ph, rg.slot_bytes, dm.err);
+    const bool ok = unit_rows_nl(m, k, c, rg.sl, rg.ph, rg.slot_bytes, dm.err, waited);
     rg.next();
     if (ok && threadIdx.x == kFeeder) feed_issue(sm, rg.nslots, rg.slot_bytes);
     return ok;
@@ -973,9 +982,10 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
         cp_async_wait_all();  // the norm weights, prefetched during the phase before
         cons_sync();
         const float ss = poll_stage(dm.ll_x, E, tag_in, sm.xv, q8 ? sm.xq8 : nullptr, sm.nrm, dm.err);
-        if (cons_or(ss < 0.f)) return false;
+        norm_partial(ss, sm);
+        // one barrier for the activations, the norm partials and the first unit's slot
+        if (cons_or(ss < 0.f || !slot_wait(sm.full, rg.sl, rg.ph, dm.err))) return false;
         tk.tr.stamp(ev, 1);
-        norm_sums(ss, sm);
     }
     const float nsc = norm_scale(dm, sm);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
@@ -983,7 +993,7 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
         const int seg = t < nq ? 0 : t < nq + nk ? 1 : 2;
         const QMat &m = seg == 0 ? L.q : seg == 1 ? L.k : L.v;
         const int lt = seg == 0 ? t : seg == 1 ? t - nq : t - nq - nk;
-        if (!unit_rows(dm, m, 1, sm, rg)) return false;
+        if (!unit_rows(dm, m, 1, sm, rg, l > 0 && t == a)) return false;
         if (threadIdx.x < 8) {
             const int r = threadIdx.x, row = lt * 8 + r;
             const float *pre = sm.pre + 4 * ((t - a) * 8);
@@ -1192,13 +1202,14 @@ __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &s
     tk.tr.stamp(ev, 0);
     const uint32_t tatt = tag_of(tk.epoch, dm.layers, l, PH_ATT);
     if (cons_or(!poll_stage_res(dm.ll_att, dm.embd, tatt, sm.xv, L.o.type == 8 ? sm.xq8 : nullptr,
-                                dm.ll_x + s.a * 8, (s.b - s.a) * 8, tin, sm.gate, dm.err)))
+                                dm.ll_x + s.a * 8, (s.b - s.a) * 8, tin, sm.gate, dm.err) ||
+                !slot_wait(sm.full, rg.sl, rg.ph, dm.err)))
         return false;
     tk.tr.stamp(ev, 1);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_O);
     for (int t = s.a; t < s.b; t += s.per) {
         const int k = min(s.per, s.b - t);
-        if (!unit_rows(dm, L.o, k, sm, rg)) return false;
+        if (!unit_rows(dm, L.o, k, sm, rg, t == s.a)) return false;
         if (threadIdx.x < k * 8) {
             const int row = t * 8 + threadIdx.x;
             ll_put(dm.ll_x + row, __fadd_rn(sm.gate[row - s.a * 8], sm.rows[threadIdx.x]), tag);
@@ -1222,9 +1233,9 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     cons_sync();
     const float ss =
         poll_stage(dm.ll_x, E, tin, sm.xv, L.gate.type == 8 || L.up.type == 8 ? sm.xq8 : nullptr, sm.nrm, dm.err);
-    if (cons_or(ss < 0.f)) return false;
+    norm_partial(ss, sm);
+    if (cons_or(ss < 0.f || !slot_wait(sm.full, rg.sl, rg.ph, dm.err))) return false;
     tk.tr.stamp(ev, 1);
-    norm_sums(ss, sm);
     const float nsc = norm_scale(dm, sm);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_GU);
     auto swiglu = [&](int row, float g, float u) {
@@ -1235,7 +1246,7 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     };
     if (gu_fused(L, sg, rg.slot_bytes)) {
         const int n = sg.b - sg.a;
-        if (!unit_rows(dm, L.gate, 2 * n, sm, rg)) return false;
+        if (!unit_rows(dm, L.gate, 2 * n, sm, rg, true)) return false;
         if (threadIdx.x < n * 8)
             swiglu(sg.a * 8 + threadIdx.x, __fmul_rn(sm.rows[threadIdx.x], nsc),
                    __fmul_rn(sm.rows[n * 8 + threadIdx.x], nsc));
@@ -1243,7 +1254,7 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     } else {
         for (int t = sg.a; t < sg.b; t += sg.per) {
             const int k = min(sg.per, sg.b - t);
-            if (!unit_rows(dm, L.gate, k, sm, rg)) return false;
+            if (!unit_rows(dm, L.gate, k, sm, rg, t == sg.a)) return false;
             if (threadIdx.x < k * 8) sm.gate[(t - sg.a) * 8 + threadIdx.x] = __fmul_rn(sm.rows[threadIdx.x], nsc);
             cons_sync();
         }
@@ -1270,13 +1281,14 @@ __device__ bool ph_down(const DecParams &dm, int l, const Tok &tk, const DecSmem
     const int ev = l * 5 + PH_DOWN;
     tk.tr.stamp(ev, 0);
     if (cons_or(!poll_stage_res(dm.ll_act, F, tact, sm.xv, L.down.type == 8 ? sm.xq8 : nullptr, dm.ll_x + s.a * 8,
-                                (s.b - s.a) * 8, tin, sm.gate, dm.err)))
+                                (s.b - s.a) * 8, tin, sm.gate, dm.err) ||
+                !slot_wait(sm.full, rg.sl, rg.ph, dm.err)))
         return false;
     tk.tr.stamp(ev, 1);
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_DOWN);
     for (int t = s.a; t < s.b; t += s.per) {
         const int k = min(s.per, s.b - t);
-        if (!unit_rows(dm, L.down, k, sm, rg)) return false;
+        if (!unit_rows(dm, L.down, k, sm, rg, t == s.a)) return false;
         if (threadIdx.x < k * 8) {
             const int row = t * 8 + threadIdx.x;
             ll_put(dm.ll_x + row, __fadd_rn(sm.gate[row - s.a * 8], sm.rows[threadIdx.x]), tag);
@@ -1372,9 +1384,9 @@ __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, R
         cp_async_wait_all();  // the norm weights, prefetched during the phase before
         cons_sync();
         const float ss = poll_stage(dm.ll_x, E, tin, sm.xv, dm.head.type == 8 ? sm.xq8 : nullptr, sm.nrm, dm.err);
+        norm_partial(ss, sm);
         if (cons_or(ss < 0.f)) return false;
         tk.tr.stamp(ev, 1);
-        norm_sums(ss, sm);
         const float nsc = norm_scale(dm, sm);
         for (int t = s.a; t < s.b; t += s.per)
             if (!head_unit(dm, min(s.per, s.b - t), t, nsc, sm, rg, bv, bi)) return false;
