@@ -1571,12 +1571,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
 DecConfig decode_config(const Shapes &s, int max_tile_bytes, int head_tile_bytes, int gate_rows, int qkv_rows,
                         int plan_units, int attn_positions) {
-    // A ring of 4 slots of at least 16 KB: it runs far enough ahead of the
-    // consumers, and a block of well under the 227 KB opt-in maximum leaves
-    // the SM most of its L1, which holds the threads' stack and the norm and
-    // RoPE rows each phase reads (with the maximum, this kernel ran 5 % slower).
+    // A ring of 4 slots of at least 16 KB runs far enough ahead of the
+    // consumers; the attention item's K/V rows take what is left.
     DecConfig c{};
-    const int budget = 232448 - 8192;  // the opt-in maximum per block, less margin
+    const int budget = 232448 - 1024;  // the opt-in maximum per block, less the static shared memory
     auto total = [&](int nslots, int slot, int chunk) {
         return dec_layout(nslots, slot, s.embd, s.ff, s.head_dim, s.heads, gate_rows, qkv_rows, plan_units, chunk).total;
     };
@@ -1588,16 +1586,14 @@ DecConfig decode_config(const Shapes &s, int max_tile_bytes, int head_tile_bytes
     c.slot_bytes = slot;
     c.nslots = min(4, ring / slot);
     // Positions per attention item: a head's whole context in one item when
-    // it fits saves the exchange of partials between CTAs.  By default the
-    // most (a multiple of 32, at most 256: a lane per position of a warp's
-    // share) for which the block stays within the 196 KB shared-memory
-    // carveout, less the 1 KB the runtime reserves per block, or within the
-    // size it has with 64 positions.
-    const size_t cap = attn_positions > 0 ? (size_t)budget
-                                          : std::max<size_t>(total(c.nslots, slot, 64), 196 * 1024 - 1024);
+    // it fits saves the exchange of partials between CTAs, which outweighs
+    // the L1 a full block of shared memory takes (measured: 224 positions ran
+    // 2.5 % faster than 192 on the SmolLM2 shape, whose contexts reach 256).
+    // By default the most that fit, a multiple of 32 up to 256 (a lane per
+    // position of a warp's share).
     c.chunk = 64;
     for (int k = attn_positions > 0 ? attn_positions : 256; k > 64; k -= 32)
-        if (total(c.nslots, slot, k) <= cap) {
+        if (total(c.nslots, slot, k) <= (size_t)budget) {
             c.chunk = k;
             break;
         }
