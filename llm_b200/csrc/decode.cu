@@ -105,6 +105,18 @@ __device__ __forceinline__ void ld_relaxed2(const uint64_t *p, uint64_t &a, uint
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
+// L2 loads as volatile asm: issued where written (before a wait), not sunk to their first use.
+__device__ __forceinline__ float4 ld_cg_early(const float4 *p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float2 ld_cg_early(const float2 *p) {
+    float2 v;
+    asm volatile("ld.global.cg.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ void st_relaxed(uint64_t *p, uint64_t v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -1023,6 +1035,73 @@ __device__ bool ph_qkv(const DecParams &dm, int l, const Tok &tk, const DecSmem 
     return true;
 }
 
+// The end of an attention item, after the warps' partials (V sum, max, sum
+// of exp) are in wpart and a consumer barrier: their combination, then the
+// head's output (one item), the item's partial (several), or, for the item
+// holding the current position, the merge of the head's items.
+template <int HD>
+__device__ __forceinline__ bool attn_finish(const DecParams &dm, const DecSmem &sm, const float *wpart, int h, int c,
+                                            int nch, bool has_cur, uint32_t otag) {
+    // the warps' partials combined: thread d < HD sums dimension d
+    float *own = sm.merge;  // the merging item's own partial: V sum [HD], max, sum of exp
+    const int d = threadIdx.x;
+    float cm = -FLT_MAX, cl = 0.f, co = 0.f;
+    if (d < HD) {
+#pragma unroll
+        for (int w = 0; w < kCons; ++w) cm = fmaxf(cm, wpart[w * (HD + 4) + HD]);
+#pragma unroll
+        for (int w = 0; w < kCons; ++w) {
+            const float *pw = wpart + w * (HD + 4);
+            const float f = pw[HD + 1] > 0.f ? expf(__fsub_rn(pw[HD], cm)) : 0.f;
+            cl = fmaf(f, pw[HD + 1], cl);
+            co = fmaf(f, pw[d], co);
+        }
+        const size_t pi = (size_t)h * dm.nchunk + c;  // head-major: a head's chunks are contiguous
+        if (nch == 1) ll_put(dm.ll_att + h * HD + d, __fdiv_rn(co, cl), otag);
+        else if (has_cur) own[d] = co;
+        else ll_put(dm.ll_pv + pi * HD + d, co, otag);
+        if (nch > 1 && d == 0) {
+            if (has_cur) {
+                own[HD] = cm, own[HD + 1] = cl;
+            } else {
+                ll_put(dm.ll_ml + pi * 2, cm, otag);
+                ll_put(dm.ll_ml + pi * 2 + 1, cl, otag);
+            }
+        }
+    }
+    cons_sync();
+    if (nch > 1 && has_cur) {
+        // The item holding the current position merges the head's other chunks
+        // (kernels_fused.go:150-170) in groups of up to 8, running max and sums
+        // in double, and publishes the head's output.
+        float *gpv = own + HD + 16, *gml = gpv + 8 * HD;
+        const int d = threadIdx.x;
+        double M = own[HD], Ls = own[HD + 1], O = d < HD ? (double)own[d] : 0.0;
+        for (int c0 = 0; c0 < nch - 1; c0 += 8) {
+            const int gn = min(8, nch - 1 - c0);
+            const size_t pi = (size_t)h * dm.nchunk + c0;
+            if (cons_or(!poll_two(dm.ll_pv + pi * HD, gn * HD, otag, gpv, dm.ll_ml + pi * 2, gn * 2, otag, gml, dm.err)))
+                return false;
+            if (d < HD) {
+                double Mn = M;
+                for (int k = 0; k < gn; ++k) Mn = fmax(Mn, (double)gml[2 * k]);
+                const double rs = exp(M - Mn);
+                O *= rs, Ls *= rs;
+                for (int k = 0; k < gn; ++k) {
+                    const double f = exp((double)gml[2 * k] - Mn);
+                    Ls = fma(f, (double)gml[2 * k + 1], Ls);
+                    O = fma(f, (double)gpv[k * HD + d], O);
+                }
+                M = Mn;
+            }
+            cons_sync();
+        }
+        if (d < HD) ll_put(dm.ll_att + h * HD + d, (float)(O / Ls), otag);
+    }
+    return true;
+}
+
+
 // K2: attention of the token (n = pos + 1 positions) for item (head,
 // chunk of dm.dec_chunk positions): scores, max and sum of exp, the
 // exp-weighted V sum (kernels_fused.go:82-146).  The chunk's cached K and V
@@ -1128,68 +1207,141 @@ __device__ bool ph_attn_t(const DecParams &dm, int l, const Tok &tk, int item, i
     for (int k = 0; k < VD / 2; ++k) *reinterpret_cast<float2 *>(wp + VD * lane + 2 * k) = ov[k];
     if (lane == 0) wp[HD] = mx, wp[HD + 1] = ls;
     cons_sync();
-    // the warps' partials combined: thread d < HD sums dimension d
-    float *own = sm.merge;  // the merging item's own partial: V sum [HD], max, sum of exp
-    const int d = threadIdx.x;
-    float cm = -FLT_MAX, cl = 0.f, co = 0.f;
-    if (d < HD) {
+    if (!attn_finish<HD>(dm, sm, wpart, h, c, nch, has_cur, otag)) return false;
+    tk.tr.stamp(ev, 2);
+    return true;
+}
+
+// K2 for head_dim 64: the same item with its cached K and V in registers
+// instead of shared memory.  At the item's start each lane loads the K row of
+// its position (the warp's share is at most 32 positions) and the two V
+// columns (2 lane, 2 lane + 1) of every position of the warp's share, from the
+// cache through L2; the token's q, k, v are then polled inline (a call would
+// spill those registers).  Scores, softmax and the V sum as ph_attn_t, without
+// the shared-memory traffic that bounded them.
+__device__ bool ph_attn_r64(const DecParams &dm, int l, const Tok &tk, int item, int nch, const DecSmem &sm) {
+    constexpr int HD = 64;
+    const int grp = dm.heads / dm.kv_heads;
+    const int h = item / nch, c = item % nch, kvh = h / grp;
+    const int n = tk.pos + 1, C = dm.dec_chunk;
+    const Layer &L = lay(sm, tk, l);
+    const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_QKV);
+    const uint32_t otag = tag_of(tk.epoch, dm.layers, l, PH_ATT);
+    float *qh = sm.att, *kc = sm.att + HD, *vc = sm.att + 2 * HD;
+    float *wpart = sm.att + 3 * HD;  // [8 warps][HD + 4]: V sum, then max and sum of exp
+    const int p0 = c * C, cnt = min(C, n - p0);
+    const bool has_cur = p0 + cnt == n;
+    const int nhist = has_cur ? cnt - 1 : cnt;
+    const int ev = l * 5 + PH_ATT;
+    tk.tr.stamp(ev, 0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int per = (cnt + kCons - 1) / kCons;  // positions per warp, at most 32
+    const int wp0 = warp * per, wcnt = max(0, min(per, cnt - wp0));
+    const float *kb = L.kv + (size_t)p0 * dm.kvd + kvh * HD;
+    const float *vb = kb + (size_t)dm.ctx * dm.kvd;
+    float4 kr[HD / 4];
+    float2 vr[32];
+    const int pk = wp0 + lane;
+    if (lane < wcnt && pk != nhist) {
+        const float4 *src = reinterpret_cast<const float4 *>(kb + (size_t)pk * dm.kvd);
 #pragma unroll
-        for (int w = 0; w < kCons; ++w) cm = fmaxf(cm, wpart[w * (HD + 4) + HD]);
+        for (int g = 0; g < HD / 4; ++g) kr[g] = ld_cg_early(src + g);
+    } else {
 #pragma unroll
-        for (int w = 0; w < kCons; ++w) {
-            const float *pw = wpart + w * (HD + 4);
-            const float f = pw[HD + 1] > 0.f ? expf(__fsub_rn(pw[HD], cm)) : 0.f;
-            cl = fmaf(f, pw[HD + 1], cl);
-            co = fmaf(f, pw[d], co);
-        }
-        const size_t pi = (size_t)h * dm.nchunk + c;  // head-major: a head's chunks are contiguous
-        if (nch == 1) ll_put(dm.ll_att + h * HD + d, __fdiv_rn(co, cl), otag);
-        else if (has_cur) own[d] = co;
-        else ll_put(dm.ll_pv + pi * HD + d, co, otag);
-        if (nch > 1 && d == 0) {
-            if (has_cur) {
-                own[HD] = cm, own[HD + 1] = cl;
-            } else {
-                ll_put(dm.ll_ml + pi * 2, cm, otag);
-                ll_put(dm.ll_ml + pi * 2 + 1, cl, otag);
-            }
-        }
+        for (int g = 0; g < HD / 4; ++g) kr[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    cons_sync();
-    if (nch > 1 && has_cur) {
-        // The item holding the current position merges the head's other chunks
-        // (kernels_fused.go:150-170) in groups of up to 8, running max and sums
-        // in double, and publishes the head's output.
-        float *gpv = own + HD + 16, *gml = gpv + 8 * HD;
-        const int d = threadIdx.x;
-        double M = own[HD], Ls = own[HD + 1], O = d < HD ? (double)own[d] : 0.0;
-        for (int c0 = 0; c0 < nch - 1; c0 += 8) {
-            const int gn = min(8, nch - 1 - c0);
-            const size_t pi = (size_t)h * dm.nchunk + c0;
-            if (cons_or(!poll_two(dm.ll_pv + pi * HD, gn * HD, otag, gpv, dm.ll_ml + pi * 2, gn * 2, otag, gml, dm.err)))
-                return false;
-            if (d < HD) {
-                double Mn = M;
-                for (int k = 0; k < gn; ++k) Mn = fmax(Mn, (double)gml[2 * k]);
-                const double rs = exp(M - Mn);
-                O *= rs, Ls *= rs;
-                for (int k = 0; k < gn; ++k) {
-                    const double f = exp((double)gml[2 * k] - Mn);
-                    Ls = fma(f, (double)gml[2 * k + 1], Ls);
-                    O = fma(f, (double)gpv[k * HD + d], O);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        vr[j] = j < wcnt && wp0 + j != nhist
+                    ? ld_cg_early(reinterpret_cast<const float2 *>(vb + (size_t)(wp0 + j) * dm.kvd) + lane)
+                    : make_float2(0.f, 0.f);
+    // q (and k, v when the item holds the current position): a thread per pair of words
+    bool ok = true;
+    {
+        constexpr int NPQ = HD / 2;
+        const int np = has_cur ? 3 * NPQ : NPQ, i = threadIdx.x;
+        if (i < np) {
+            const int sg = i / NPQ, j = i % NPQ;
+            const uint64_t *src = (sg == 0 ? dm.ll_q + h * HD : sg == 1 ? dm.ll_k + kvh * HD : dm.ll_v + kvh * HD) + 2 * j;
+            float *dst = (sg == 0 ? qh : sg == 1 ? kc : vc) + 2 * j;
+            uint64_t a, b;
+            ld_relaxed2(src, a, b);
+            if ((uint32_t)(a >> 32) != tag || (uint32_t)(b >> 32) != tag) {
+                const uint64_t t0 = gtimer();
+                unsigned spins = 0;
+                while (true) {
+                    ld_relaxed2(src, a, b);
+                    if ((uint32_t)(a >> 32) == tag && (uint32_t)(b >> 32) == tag) break;
+                    if ((++spins & 255) == 0) {
+                        if (read_err(dm.err)) {
+                            ok = false;
+                            break;
+                        }
+                        if (gtimer() - t0 > kWaitNs) {
+                            atomicExch(dm.err, DEV_TAG_TIMEOUT);
+                            ok = false;
+                            break;
+                        }
+                    }
                 }
-                M = Mn;
             }
-            cons_sync();
+            dst[0] = __uint_as_float((uint32_t)a), dst[1] = __uint_as_float((uint32_t)b);
         }
-        if (d < HD) ll_put(dm.ll_att + h * HD + d, (float)(O / Ls), otag);
     }
+    if (cons_or(!ok)) return false;
+    tk.tr.stamp(ev, 1);
+    if (lane < wcnt && pk == nhist) {  // the current position's K row came with the poll
+#pragma unroll
+        for (int g = 0; g < HD / 4; ++g) kr[g] = *reinterpret_cast<const float4 *>(kc + 4 * g);
+    }
+    // scores: a lane per position
+    float sc = -FLT_MAX;
+    if (lane < wcnt) {
+        float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int g = 0; g < HD / 4; ++g) {
+            const float4 k4 = kr[g];
+            const float4 q4 = *reinterpret_cast<const float4 *>(qh + 4 * g);
+            a01 = __ffma2_rn(make_float2(q4.x, q4.y), make_float2(k4.x, k4.y), a01);
+            a23 = __ffma2_rn(make_float2(q4.z, q4.w), make_float2(k4.z, k4.w), a23);
+        }
+        sc = __fmul_rn((a01.x + a01.y) + (a23.x + a23.y), dm.scale);
+    }
+    float mx = sc;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    const float e = lane < wcnt ? expf(__fsub_rn(sc, mx)) : 0.f;  // cpu.go:321
+    // the V sum over the warp's positions, and the sum of exp alongside: all
+    // 32 slots without branches (past the share both the weight and the
+    // registers are 0), in two chains; the current position's V column came
+    // with the poll and is added last (its weight is in the sum already)
+    float2 ov0 = make_float2(0.f, 0.f), ov1 = make_float2(0.f, 0.f);
+    float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+        const float w0 = __shfl_sync(kFull, e, j), w1 = __shfl_sync(kFull, e, j + 1);
+        ov0 = __ffma2_rn(make_float2(w0, w0), vr[j], ov0);
+        ov1 = __ffma2_rn(make_float2(w1, w1), vr[j + 1], ov1);
+        ls0 += w0, ls1 += w1;
+    }
+    float2 ov = make_float2(ov0.x + ov1.x, ov0.y + ov1.y);
+    float ls = ls0 + ls1;
+    const int jc = nhist - wp0;
+    if (jc >= 0 && jc < wcnt) {
+        const float w = __shfl_sync(kFull, e, jc);
+        ov = __ffma2_rn(make_float2(w, w), *reinterpret_cast<const float2 *>(vc + 2 * lane), ov);
+    }
+    float *wp = wpart + warp * (HD + 4);
+    *reinterpret_cast<float2 *>(wp + 2 * lane) = ov;
+    if (lane == 0) wp[HD] = mx, wp[HD + 1] = ls;
+    cons_sync();
+    if (!attn_finish<HD>(dm, sm, wpart, h, c, nch, has_cur, otag)) return false;
     tk.tr.stamp(ev, 2);
     return true;
 }
 
 __device__ bool ph_attn(const DecParams &dm, int l, const Tok &tk, int item, int nch, const DecSmem &sm) {
-    return dm.head_dim == 128 ? ph_attn_t<128>(dm, l, tk, item, nch, sm) : ph_attn_t<64>(dm, l, tk, item, nch, sm);
+    return dm.head_dim == 128 ? ph_attn_t<128>(dm, l, tk, item, nch, sm) : ph_attn_r64(dm, l, tk, item, nch, sm);
 }
 
 // K3: x += Wo att (cpu.go:336-339).

@@ -167,9 +167,10 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     l.gate = p, p += 4 * (size_t)gate_rows;
     // an attention item's history K rows [dec_chunk][head_dim + 4] and V rows
     // [dec_chunk][head_dim] share the bytes of the matrix phases' vectors
-    // above (no phase uses both)
+    // above (no phase uses both); with head_dim 64 the item keeps them in
+    // registers
     l.kvs = l.xv;
-    const size_t kv_end = l.kvs + 4 * (size_t)dec_chunk * (2 * head_dim + 4);
+    const size_t kv_end = l.kvs + (head_dim == 64 ? 0 : 4 * (size_t)dec_chunk * (2 * head_dim + 4));
     p = p > kv_end ? p : kv_end;
     p = (p + 15) / 16 * 16;
     l.red = p, p += 4 * 64;
