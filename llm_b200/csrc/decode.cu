@@ -219,39 +219,6 @@ __device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Fenced grid barrier among the consumer threads of all CTAs.
-__device__ bool grid_sync_cons(GridBarrier *bar, int *err) {
-    __shared__ int ok;
-    cons_sync();
-    if (threadIdx.x == 0) {
-        ok = 1;
-        const unsigned g = ld_acquire(&bar->gen);
-        __threadfence();
-        const unsigned arrived = atomicAdd(&bar->count, 1u);
-        if (arrived == gridDim.x - 1) {
-            bar->count = 0;
-            __threadfence();
-            st_release(&bar->gen, g + 1);
-        } else {
-            const uint64_t t0 = gtimer();
-            while (ld_acquire(&bar->gen) == g) {
-                if (read_err(err)) {
-                    ok = 0;
-                    break;
-                }
-                if (gtimer() - t0 > kWaitNs) {
-                    atomicExch(err, DEV_BARRIER_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        __threadfence();
-    }
-    cons_sync();
-    return ok != 0;
-}
-
 __device__ __forceinline__ float b2f(uint32_t v, int k) {
     return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | k));
 }
@@ -773,7 +740,7 @@ __device__ __forceinline__ uint32_t tag_of(uint32_t epoch, int layers, int l, in
     return epoch * (uint32_t)(8 * (layers + 1)) + (uint32_t)(8 * (l + 1) + ph) + 1u;
 }
 
-enum { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4 };
+enum { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_HEAD = 5 };
 
 // Gate and up tiles of a CTA travel as one unit when they have one format and
 // fit one slot (the feeder copies both ranges into the slot).
@@ -1558,18 +1525,35 @@ __device__ bool ph_head(const DecParams &dm, const Tok &tk, const DecSmem &sm, R
             const int i = __float_as_int(sm.red[kCons + k]);
             if (better(v, i, bv, bi)) bv = v, bi = i;
         }
-        dm.am_part[blockIdx.x] = make_float2(bv, __int_as_float(bi));
+        // the token's argmax partial, released: every CTA's writes of the token
+        // (its KV rows) are visible to a CTA that has read it and fenced
+        __threadfence();
+        uint64_t *dst = dm.ll_am + ((size_t)(tk.epoch & 1) * gridDim.x + blockIdx.x) * 2;
+        const uint32_t tag = tag_of(tk.epoch, dm.layers, dm.layers - 1, PH_HEAD);
+        ll_put(dst, bv, tag);
+        ll_put(dst + 1, __int_as_float(bi), tag);
     }
     tk.tr.stamp(ev, 2);
     return true;
 }
 
-__device__ int final_argmax(const DecParams &dm, const DecSmem &sm) {
+// The token: the argmax over every CTA's partial (polled, then fenced, so
+// that the KV rows the CTAs wrote for this token are visible to this CTA's
+// next reads); -1 on a device error.  Partials alternate between two buffers
+// by token, and every CTA reads them all before its next token, so none is
+// overwritten before it is read.
+__device__ int argmax_partials(const DecParams &dm, const Tok &tk, const DecSmem &sm) {
+    const uint32_t tag = tag_of(tk.epoch, dm.layers, dm.layers - 1, PH_HEAD);
+    const Seg seg[1] = {{dm.ll_am + (size_t)(tk.epoch & 1) * gridDim.x * 2, 2 * (int)gridDim.x, tag, sm.xv}};
+    const bool ok = poll_segs(seg, dm.err);
+    __threadfence();
+    if (cons_or(!ok)) return -1;
     float bv = -FLT_MAX;
     int bi = 0x7fffffff;
     for (int i = threadIdx.x; i < (int)gridDim.x; i += kConsThreads) {
-        const float2 p = __ldcg(dm.am_part + i);
-        if (better(p.x, __float_as_int(p.y), bv, bi)) bv = p.x, bi = __float_as_int(p.y);
+        const float v = sm.xv[2 * i];
+        const int ix = __float_as_int(sm.xv[2 * i + 1]);
+        if (better(v, ix, bv, bi)) bv = v, bi = ix;
     }
     for (int o = 16; o; o >>= 1) {
         const float ov = __shfl_xor_sync(kFull, bv, o);
@@ -1577,7 +1561,6 @@ __device__ int final_argmax(const DecParams &dm, const DecSmem &sm) {
         if (better(ov, oi, bv, bi)) bv = ov, bi = oi;
     }
     const int w = threadIdx.x >> 5;
-    cons_sync();
     if ((threadIdx.x & 31) == 0) sm.red[w] = bv, sm.red[kCons + w] = __int_as_float(bi);
     cons_sync();
     if (threadIdx.x == 0) {
@@ -1594,7 +1577,7 @@ __device__ int final_argmax(const DecParams &dm, const DecSmem &sm) {
 
 // The token loop of the persistent kernel (returns early on a device error,
 // which dm.err records).
-__device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *bar, int ntok, const DecSmem &sm,
+__device__ __forceinline__ void decode_tokens(const DecParams &dm, int ntok, const DecSmem &sm,
                                               Ring &rg) {
     Tok tk;
     tk.pos = (int)__ldcg(dm.state), tk.step = (int)__ldcg(dm.state + 1);
@@ -1646,12 +1629,12 @@ __device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *
         }
         if (!ph_head(dm, tk, sm, rg)) return;
         tk.tr.stamp(dm.layers * 5 + 1, 0);
-        if (!grid_sync_cons(bar, dm.err)) return;
+        const int tok = argmax_partials(dm, tk, sm);
+        if (tok < 0) return;
         tk.tr.stamp(dm.layers * 5 + 1, 2);
-        tk.tok = final_argmax(dm, sm);
+        tk.tok = tok;
         tk.pos++, tk.step++, tk.epoch++;
         if (blockIdx.x == 0 && threadIdx.x == 0) dm.tokens[tk.step] = tk.tok;
-        // the partials are read before any CTA writes the next token's (its head comes after every phase)
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         dm.state[0] = tk.pos;
@@ -1661,7 +1644,7 @@ __device__ __forceinline__ void decode_tokens(const DecParams &dm, GridBarrier *
 }
 
 __global__ void __launch_bounds__(kDecThreads, 1)
-    k_decode2(const __grid_constant__ DecParams dm, GridBarrier *bar, int ntok, int nslots, int slot_bytes) {
+    k_decode2(const __grid_constant__ DecParams dm, int ntok, int nslots, int slot_bytes) {
     extern __shared__ __align__(128) uint8_t dsm[];
     DecSmem sm;
     {
@@ -1714,7 +1697,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     if (threadIdx.x == kFeeder)
         for (int i = 0; i < nslots; ++i) feed_issue(sm, nslots, slot_bytes);
     Ring rg{nslots, slot_bytes, 0u, 0, 0u};
-    decode_tokens(dm, bar, ntok, sm, rg);
+    decode_tokens(dm, ntok, sm, rg);
     cp_async_wait_all();  // descriptor copies of layers past the launch's last
     if (threadIdx.x == kFeeder) feed_drain(sm, nslots, rg.u);
 }
@@ -1754,7 +1737,7 @@ DecConfig decode_config(const Shapes &s, int max_tile_bytes, int head_tile_bytes
     return c;
 }
 
-cudaError_t launch_decode2(const DecParams &dm, const DecConfig &c, GridBarrier *bar, int ntok, int ctas,
+cudaError_t launch_decode2(const DecParams &dm, const DecConfig &c, int ntok, int ctas,
                            cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(k_decode2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
     if (e != cudaSuccess) return e;
@@ -1768,7 +1751,7 @@ cudaError_t launch_decode2(const DecParams &dm, const DecConfig &c, GridBarrier 
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_decode2, dm, bar, ntok, c.nslots, c.slot_bytes);
+    return cudaLaunchKernelEx(&cfg, k_decode2, dm, ntok, c.nslots, c.slot_bytes);
 }
 
 cudaError_t launch_feed_plan(const DecParams &dm, int slot_bytes, FeedUnit *plan, int *count, int ctas,

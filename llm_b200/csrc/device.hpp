@@ -106,6 +106,7 @@ struct ModelHeader {
 
     // the persistent decode kernel's tagged activations ({f32 value, u32 tag})
     uint64_t *ll_x, *ll_q, *ll_k, *ll_v, *ll_att, *ll_act, *ll_pv, *ll_ml;
+    uint64_t *ll_am;     // per token parity and CTA: the head's argmax partial {value, index}
     uint32_t *ll_epoch;  // tokens decoded so far by the persistent kernel (makes tags unique across calls)
     int dec_gate_rows;   // gate rows of the largest gate/up share of a CTA
     int dec_qkv_rows;    // rows of the largest QKV share of a CTA

@@ -61,7 +61,6 @@ struct Model {
     Shapes sh{};
     DevModel hdm{};  // host copy of the device description
     DevModel *dm = nullptr;
-    GridBarrier *bar = nullptr;
     cudaStream_t st = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr, ev3 = nullptr;
     cudaEvent_t lev[4][3] = {};  // per decode launch: start, end, tokens copied
@@ -389,7 +388,6 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     if (!(d.gam = m.alloc<float2>((size_t)pm * ((d.head.rows + 63) / 64) * 8, err))) return err;
     if (!(d.am_count = m.alloc<uint32_t>(kMaxPrefill * 4, err))) return err;
     if (!(d.err = m.alloc<int>(4, err))) return err;
-    if (!(m.bar = m.alloc<GridBarrier>(sizeof(GridBarrier), err))) return err;
     // the persistent decode kernel: tagged activations and its ring configuration
     if (!(d.ll_x = m.alloc<uint64_t>((size_t)E * 8, err))) return err;
     if (!(d.ll_q = m.alloc<uint64_t>((size_t)E * 8, err))) return err;
@@ -399,6 +397,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     if (!(d.ll_act = m.alloc<uint64_t>((size_t)F * 8, err))) return err;
     if (!(d.ll_pv = m.alloc<uint64_t>((size_t)c.heads * d.nchunk * c.head_dim * 8, err))) return err;
     if (!(d.ll_ml = m.alloc<uint64_t>((size_t)c.heads * d.nchunk * 2 * 8, err))) return err;
+    if (!(d.ll_am = m.alloc<uint64_t>((size_t)2 * m.persistent_ctas * 2 * 8, err))) return err;
     if (!(d.ll_epoch = m.alloc<uint32_t>(4, err))) return err;
     d.trace_events = c.layers * 5 + 2;
     if (g_decode_trace.load() &&
@@ -568,7 +567,7 @@ cudaError_t reset_tags(Model &m) {
         {d.ll_x, (size_t)E * 8}, {d.ll_q, (size_t)E * 8}, {d.ll_k, (size_t)kvd * 8}, {d.ll_v, (size_t)kvd * 8},
         {d.ll_att, (size_t)E * 8}, {d.ll_act, (size_t)F * 8},
         {d.ll_pv, (size_t)m.cfg.heads * d.nchunk * m.cfg.head_dim * 8}, {d.ll_ml, (size_t)m.cfg.heads * d.nchunk * 2 * 8},
-        {d.ll_epoch, 4}};
+        {d.ll_am, (size_t)2 * m.persistent_ctas * 2 * 8}, {d.ll_epoch, 4}};
     for (const auto &b : bufs) {
         const cudaError_t e = cudaMemsetAsync(b.first, 0, b.second, m.st);
         if (e != cudaSuccess) return e;
@@ -587,7 +586,7 @@ Error decode(Model &m, int cnt) {
             CUDA_TRY(reset_tags(m));
             m.ll_tokens = 0;
         }
-        CUDA_TRY(launch_decode2(*m.dp, m.dec, m.bar, cnt, m.persistent_ctas, m.st));
+        CUDA_TRY(launch_decode2(*m.dp, m.dec, cnt, m.persistent_ctas, m.st));
         m.ll_tokens += cnt;
         m.stats.dispatches++;
     } else {

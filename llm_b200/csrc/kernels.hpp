@@ -16,11 +16,6 @@ enum DeviceError : int {
     DEV_RING_TIMEOUT = 4,     // a weight slot did not fill or drain in time
 };
 
-struct GridBarrier {
-    unsigned int count;
-    unsigned int gen;
-};
-
 // Host copy of what launch shapes need.
 struct Shapes {
     int embd, ff, heads, kv_heads, head_dim, kvd, vocab, ctx, layers, nchunk;
@@ -89,7 +84,7 @@ DecConfig decode_config(const Shapes &s, int max_tile_bytes, int head_tile_bytes
 // Each CTA's weight units of one token for the persistent kernel (its grid: ctas).
 cudaError_t launch_feed_plan(const DecParams &dm, int slot_bytes, FeedUnit *plan, int *count, int ctas,
                              cudaStream_t st);
-cudaError_t launch_decode2(const DecParams &dm, const DecConfig &c, GridBarrier *bar, int ntok, int ctas,
+cudaError_t launch_decode2(const DecParams &dm, const DecConfig &c, int ntok, int ctas,
                            cudaStream_t st);
 int decode2_ctas_per_sm(const DecConfig &c);
 
