@@ -1014,15 +1014,25 @@ __device__ __forceinline__ bool attn_finish(const DecParams &dm, const DecSmem &
     const int d = threadIdx.x;
     float cm = -FLT_MAX, cl = 0.f, co = 0.f;
     if (d < HD) {
-#pragma unroll
-        for (int w = 0; w < kCons; ++w) cm = fmaxf(cm, wpart[w * (HD + 4) + HD]);
+        // a warp without positions left max -FLT_MAX, sum 0 and a zero V sum:
+        // its factor is exp(-huge) = 0
+        float2 ml[kCons];
+        float ow[kCons];
 #pragma unroll
         for (int w = 0; w < kCons; ++w) {
-            const float *pw = wpart + w * (HD + 4);
-            const float f = pw[HD + 1] > 0.f ? expf(__fsub_rn(pw[HD], cm)) : 0.f;
-            cl = fmaf(f, pw[HD + 1], cl);
-            co = fmaf(f, pw[d], co);
+            ml[w] = *reinterpret_cast<const float2 *>(wpart + w * (HD + 4) + HD);
+            ow[w] = wpart[w * (HD + 4) + d];
         }
+#pragma unroll
+        for (int w = 0; w < kCons; ++w) cm = fmaxf(cm, ml[w].x);
+        float cl1 = 0.f, co1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < kCons; w += 2) {
+            const float f0 = expf(__fsub_rn(ml[w].x, cm)), f1 = expf(__fsub_rn(ml[w + 1].x, cm));
+            cl = fmaf(f0, ml[w].y, cl), cl1 = fmaf(f1, ml[w + 1].y, cl1);
+            co = fmaf(f0, ow[w], co), co1 = fmaf(f1, ow[w + 1], co1);
+        }
+        cl += cl1, co += co1;
         const size_t pi = (size_t)h * dm.nchunk + c;  // head-major: a head's chunks are contiguous
         if (nch == 1) ll_put(dm.ll_att + h * HD + d, __fdiv_rn(co, cl), otag);
         else if (has_cur) own[d] = co;
@@ -1036,8 +1046,9 @@ __device__ __forceinline__ bool attn_finish(const DecParams &dm, const DecSmem &
             }
         }
     }
+    if (nch == 1) return true;  // nothing reads the partials' bytes before the next item's own barriers
     cons_sync();
-    if (nch > 1 && has_cur) {
+    if (has_cur) {
         // The item holding the current position merges the head's other chunks
         // (kernels_fused.go:150-170) in groups of up to 8, running max and sums
         // in double, and publishes the head's output.
@@ -1265,14 +1276,18 @@ __device__ bool ph_attn_r64(const DecParams &dm, int l, const Tok &tk, int item,
     float sc = -FLT_MAX;
     if (lane < wcnt) {
         float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+        float2 b01 = make_float2(0.f, 0.f), b23 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int g = 0; g < HD / 4; ++g) {
-            const float4 k4 = kr[g];
+        for (int g = 0; g < HD / 4; g += 2) {
+            const float4 k4 = kr[g], k5 = kr[g + 1];
             const float4 q4 = *reinterpret_cast<const float4 *>(qh + 4 * g);
+            const float4 q5 = *reinterpret_cast<const float4 *>(qh + 4 * g + 4);
             a01 = __ffma2_rn(make_float2(q4.x, q4.y), make_float2(k4.x, k4.y), a01);
             a23 = __ffma2_rn(make_float2(q4.z, q4.w), make_float2(k4.z, k4.w), a23);
+            b01 = __ffma2_rn(make_float2(q5.x, q5.y), make_float2(k5.x, k5.y), b01);
+            b23 = __ffma2_rn(make_float2(q5.z, q5.w), make_float2(k5.z, k5.w), b23);
         }
-        sc = __fmul_rn((a01.x + a01.y) + (a23.x + a23.y), dm.scale);
+        sc = __fmul_rn(((a01.x + a01.y) + (a23.x + a23.y)) + ((b01.x + b01.y) + (b23.x + b23.y)), dm.scale);
     }
     float mx = sc;
 #pragma unroll
