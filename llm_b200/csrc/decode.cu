@@ -257,12 +257,18 @@ __device__ __forceinline__ int split_at(int T, int i, int P) { return (int)((uns
 // phase they delayed its first poll.)
 enum { SK_QKV = 0, SK_O, SK_GU, SK_DOWN, SK_HEAD, SK_N };
 struct ShareTab {
-    int a[SK_N], b[SK_N];  // tiles [a, b) of the kind (QKV: of q, k, v in turn)
+    int a[SK_N], b[SK_N];  // tiles [a, b) of the kind (QKV: of q, k, v in turn; down: half tiles if down_half)
     int per[SK_N][3];      // tiles per unit by format: Q4_0, Q4_1, Q8_0
+    int down_half;         // the down product in half tiles (4 rows) per CTA
 };
 static_assert(sizeof(ShareTab) <= 128, "the shared-memory layout reserves 128 bytes");
 
 __device__ __forceinline__ int fmt_ix(int type) { return type == 8 ? 2 : type == 3 ? 1 : 0; }
+
+// The down product runs in half tiles (4 rows, two warps per row) when the
+// grid has a CTA for each: its rows are the longest (ff weights), and half the
+// CTAs had no down rows.
+__device__ __forceinline__ bool down_halves(const QMat &down, int ncta) { return 2 * (down.rows >> 3) <= ncta; }
 
 __device__ __forceinline__ Share share(const QMat &m, int cta, int ncta, int slot_bytes) {
     const int T = m.rows >> 3;
@@ -390,11 +396,13 @@ __device__ __forceinline__ float dot_tile(int type, const uint8_t *tile, int nb,
 // blocks), summed over the warp: every lane returns the row's value.  Used
 // for units of fewer tiles than warps, where each warp takes whole rows and
 // no partial sums cross warps.
-__device__ __forceinline__ float dot_row(int type, const uint8_t *tile, int nb, int r, const DecSmem &sm, int lane) {
+__device__ __forceinline__ float dot_row(int type, const uint8_t *tile, int nb, int r, const DecSmem &sm, int lane,
+                                         int b0 = 0, int b1 = -1) {
+    if (b1 < 0) b1 = nb;
     float acc = 0.f;
     if (type == 8) {
         const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 256);
-        for (int b = lane; b < nb; b += 32) {
+        for (int b = b0 + lane; b < b1; b += 32) {
             const uint4 *qp = reinterpret_cast<const uint4 *>(tile + ((size_t)b * 8 + r) * 32);
             const float4 *xp = reinterpret_cast<const float4 *>(sm.xq8 + b * kXB);
             const float d = __half2float(dp[b * 8 + r]);
@@ -417,7 +425,7 @@ __device__ __forceinline__ float dot_row(int type, const uint8_t *tile, int nb, 
         const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)nb * 128);
         const float off = type == 3 ? 8388608.f : 8388616.f;
         const float2 o2 = make_float2(-off, -off);
-        for (int b = lane; b < nb; b += 32) {
+        for (int b = b0 + lane; b < b1; b += 32) {
             const uint4 q = *reinterpret_cast<const uint4 *>(tile + ((size_t)b * 8 + r) * 16);
             const float4 *xp = reinterpret_cast<const float4 *>(sm.xv + b * kXB);  // pairs (x_j, x_j+16)
             const float d = __half2float(dp[b * 8 + r]);
@@ -821,6 +829,13 @@ __device__ bool feed_next(const DecParams &dm, Feed &f, int ntok, int slot_bytes
                 continue;
             }
             if (share_unit(L.gate, sg, f.t, s1, n1)) return true;
+        } else if (f.st == 4 && down_halves(L.down, ncta)) {
+            if (f.t == 0 && cta < 2 * (L.down.rows >> 3)) {  // half tile cta: the whole tile travels
+                s1 = L.down.tiles + (size_t)(cta >> 1) * L.down.tile_bytes;
+                n1 = (unsigned)L.down.tile_bytes;
+                f.t = 1;
+                return true;
+            }
         } else {
             const QMat &m = f.st == 1 ? L.o : f.st == 3 ? L.up : L.down;
             if (share_unit(m, share(m, cta, ncta, slot_bytes), f.t, s1, n1)) return true;
@@ -1406,10 +1421,43 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
 }
 
 // K5: x += Wdown act (cpu.go:347-350).
+// The down product on a half tile: rows r0..r0+3 of tile t, two warps per row
+// (each half of the blocks), the residual add in the epilogue.
+__device__ bool ph_down_half(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg, int hh) {
+    const Layer &L = lay(sm, tk, l);
+    const QMat &m = L.down;
+    const int t = hh >> 1, r0 = (hh & 1) * 4, row0 = t * 8 + r0;
+    const uint32_t tact = tag_of(tk.epoch, dm.layers, l, PH_GU), tin = tag_of(tk.epoch, dm.layers, l, PH_O);
+    const int ev = l * 5 + PH_DOWN;
+    tk.tr.stamp(ev, 0);
+    if (cons_or(!poll_stage_res(dm.ll_act, dm.ff, tact, sm.xv, m.type == 8 ? sm.xq8 : nullptr, dm.ll_x + row0, 4,
+                                tin, sm.gate, dm.err) ||
+                !slot_wait(sm.full, rg.sl, rg.ph, dm.err)))
+        return false;
+    tk.tr.stamp(ev, 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint8_t *slot = sm.ring + (size_t)rg.sl * rg.slot_bytes;
+    const int hb = m.nb >> 1, b0 = (warp & 1) * hb, b1 = (warp & 1) ? m.nb : hb;
+    const float a = dot_row(m.type, slot, m.nb, r0 + (warp >> 1), sm, lane, b0, b1);
+    float *part = reinterpret_cast<float *>(sm.part);
+    if (lane == 0) part[warp] = a;
+    cons_sync();  // the slot is read: the feeder may refill it
+    rg.next();
+    if (threadIdx.x == kFeeder) feed_issue(sm, rg.nslots, rg.slot_bytes);
+    if (threadIdx.x < 4) {
+        const float v = __fadd_rn(part[2 * threadIdx.x], part[2 * threadIdx.x + 1]);
+        ll_put(dm.ll_x + row0 + threadIdx.x, __fadd_rn(sm.gate[threadIdx.x], v),
+               tag_of(tk.epoch, dm.layers, l, PH_DOWN));
+    }
+    tk.tr.stamp(ev, 2);
+    return true;
+}
+
 __device__ bool ph_down(const DecParams &dm, int l, const Tok &tk, const DecSmem &sm, Ring &rg) {
     const Layer &L = lay(sm, tk, l);
     const Share s = share_of(sm, SK_DOWN, L.down);
     if (s.b <= s.a) return true;
+    if (sm.st->down_half) return ph_down_half(dm, l, tk, sm, rg, s.a);
     const int F = dm.ff;
     const uint32_t tact = tag_of(tk.epoch, dm.layers, l, PH_GU), tin = tag_of(tk.epoch, dm.layers, l, PH_O);
     const int ev = l * 5 + PH_DOWN;
@@ -1691,10 +1739,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         const QMat &m = kind == SK_QKV ? L0.q : kind == SK_O ? L0.o : kind == SK_GU ? L0.gate
                                              : kind == SK_DOWN ? L0.down : dm.head;
         if (what == 0) {
-            const int T = kind == SK_QKV ? (L0.q.rows + L0.k.rows + L0.v.rows) >> 3 : m.rows >> 3;
+            const bool half = kind == SK_DOWN && down_halves(m, gridDim.x);
+            const int T = kind == SK_QKV ? (L0.q.rows + L0.k.rows + L0.v.rows) >> 3 : (m.rows >> 3) << (half ? 1 : 0);
             const int P = min((int)gridDim.x, T), cta = blockIdx.x;
             sm.st->a[kind] = cta < P ? split_at(T, cta, P) : 0;
             sm.st->b[kind] = cta < P ? split_at(T, cta + 1, P) : 0;
+            if (kind == SK_DOWN) sm.st->down_half = half;
         } else {
             const int type = what == 1 ? 2 : what == 2 ? 3 : 8;  // formats in fmt_ix order
             sm.st->per[kind][what - 1] = max(1, min(kConsThreads / 8, slot_bytes / tile_bytes_of(type, m.nb)));
