@@ -9,19 +9,22 @@
 //     them and refills each slot as soon as its unit is consumed.  Weights do
 //     not depend on activations, so the stream runs ahead across phases,
 //     layers and tokens as far as the ring allows;
-//   - the 8 warps compute.  Every tile's blocks are split across the warps
-//     (paired f32 math); the partials meet in shared memory and shuffles in
-//     a fixed order, so results are deterministic.
+//   - the 8 warps compute (paired f32 math): a row per warp for units of one
+//     tile, a tile's blocks split across warps for larger units; partials
+//     meet in shared memory and shuffles in a fixed order, so results are
+//     deterministic.
 //
 // Activations move between CTAs as 64-bit words {f32 value, u32 tag}
 // written and polled with relaxed GPU-scope accesses (a value and its tag
 // are one single-copy-atomic store, so a reader that sees the tag sees the
 // value): each CTA waits only for the vector it needs, with no grid-wide
 // barrier between phases.  A tag is unique per (token, layer, phase)
-// across calls (a device epoch counter).  One fenced grid barrier per token
-// publishes the argmax partials and the token's KV-cache rows.
+// across calls (a device epoch counter).  A token ends with each CTA's argmax
+// partial published the same way after a release fence, and read by every
+// CTA, then an acquire fence: that also makes the token's KV-cache rows
+// visible to the next token's attention, with no grid-wide barrier.
 //
-// Every wait (mbarrier, tag poll, grid barrier) is bounded: past its limit
+// Every wait (mbarrier, tag poll) is bounded: past its limit
 // the kernel records an error in DevModel::err and returns; the CTA first
 // waits (bounded) for its weight copies in flight.
 #include <cuda_fp16.h>

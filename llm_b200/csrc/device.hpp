@@ -122,7 +122,7 @@ struct ModelHeader {
     // the phase's entry, when its input was ready, at its exit, and + 3 the
     // SM cycles it waited for weight slots; events are
     // 5 per layer (QKV, attention, output, gate/up, down), then head, then
-    // the token's grid barrier.  Recorded for the first token of a launch.
+    // the token's argmax exchange.  Recorded for the first token of a launch.
     uint64_t *trace;
     int trace_events;
 };

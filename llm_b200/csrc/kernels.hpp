@@ -10,7 +10,7 @@ namespace llmb {
 // Device error codes written to DevModel::err.
 enum DeviceError : int {
     DEV_OK = 0,
-    DEV_BARRIER_TIMEOUT = 1,  // a grid barrier waited longer than its limit
+    DEV_BARRIER_TIMEOUT = 1,  // reserved: a grid-wide barrier waited longer than its limit (none is used now)
     DEV_CONTEXT_FULL = 2,     // a token past the context
     DEV_TAG_TIMEOUT = 3,      // a tagged activation did not arrive in time
     DEV_RING_TIMEOUT = 4,     // a weight slot did not fill or drain in time
