@@ -656,11 +656,6 @@ struct UnitCtx {
     float *xv, *xq8, *part, *rows;
 };
 
-// Computes the rows of one unit (k tiles of matrix m) into c.rows[k * 8]
-// (row i of the unit).  All consumer warps take part: with k >= 8 each warp
-// takes whole tiles, otherwise every tile's blocks are split across the
-// warps, whose partials meet through shared memory and three shuffles, in a
-// fixed order.
 // This thread's wait for a ring slot's fill (false: timed out or a device
 // error; the caller's consumer barrier makes the outcome uniform).
 __device__ __forceinline__ bool slot_wait(uint64_t *full, int sl, unsigned ph, int *err) {
@@ -682,6 +677,11 @@ __device__ __forceinline__ bool slot_wait(uint64_t *full, int sl, unsigned ph, i
     return ok;
 }
 
+// Computes the rows of one unit (k tiles of matrix m) into c.rows[k * 8]
+// (row i of the unit).  All consumer warps take part: with k >= 8 each warp
+// takes whole tiles; with k == 1 warp w takes row w, a block per lane;
+// otherwise every tile's blocks are split across the warps, whose partials
+// meet through shared memory and three shuffles, in a fixed order.
 // waited: the caller has waited for the slot and passed a consumer barrier since.
 __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const UnitCtx &c, const int sl,
                                              const unsigned ph, const int slot_bytes, int *err, bool waited) {
@@ -909,9 +909,8 @@ struct Tok {
     Trace tr;  // this token's timeline (first token of a launch only)
 };
 
-// Per-layer descriptors are read from shared memory: the kernel parameter's
-// copy sits in the constant bank, where the first read of a layer's fields in
-// a phase missed the constant cache (a few hundred ns at every phase).  Layer
+// Per-layer descriptors are read from shared memory rather than from the
+// kernel parameter's constant bank (measured a little faster).  Layer
 // g % layers of the launch's sequence goes to buffer g % 3, copied two layers
 // ahead (cp.async) and waited for at the top of the layer before it.
 __device__ __forceinline__ const Layer &lay(const DecSmem &sm, const Tok &tk, int l) { return sm.lay[(tk.g0 + l) % 3]; }
