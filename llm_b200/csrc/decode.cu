@@ -212,16 +212,6 @@ __device__ __forceinline__ bool poll_two(const uint64_t *a, int na, uint32_t ta,
     return poll_segs(sg, err);
 }
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ float b2f(uint32_t v, int k) {
     return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | k));
 }
