@@ -222,7 +222,7 @@ def test_rmsnorm_and_argmax(oracle):
 # ------------------------------------------------------------ forward --
 
 
-@pytest.mark.parametrize("spec", ["tiny-llama", "tiny-mixed", "tiny-qwen2"])
+@pytest.mark.parametrize("spec", ["tiny-llama", "tiny-mixed", "tiny-qwen2", "tiny-hd128"])
 def test_forward_matches_float64(oracle, model_path, spec):
     """The oracle's Forward against the independent float64 forward over 12 tokens."""
     path = model_path(spec)
