@@ -1087,7 +1087,8 @@ __device__ __forceinline__ bool attn_finish(const DecParams &dm, const DecSmem &
 }
 
 
-// K2: attention of the token (n = pos + 1 positions) for item (head,
+// K2 (head_dim 128; head_dim 64 runs ph_attn_r64 below): attention of the
+// token (n = pos + 1 positions) for item (head,
 // chunk of dm.dec_chunk positions): scores, max and sum of exp, the
 // exp-weighted V sum (kernels_fused.go:82-146).  The chunk's cached K and V
 // rows do not depend on this token, so they are copied into shared memory
