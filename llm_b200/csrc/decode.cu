@@ -1382,7 +1382,8 @@ __device__ bool ph_gu(const DecParams &dm, int l, const Tok &tk, const DecSmem &
     const uint32_t tag = tag_of(tk.epoch, dm.layers, l, PH_GU);
     auto swiglu = [&](int row, float g, float u) {
         if (row < dm.ff) {
-            const float den = __fadd_rn(1.f, (float)exp(-(double)g));  // as cpu.go:345
+            // cpu.go:345 rounds exp in double to float; expf is within 2 ulp of that
+            const float den = __fadd_rn(1.f, expf(-g));
             ll_put(dm.ll_act + row, __fmul_rn(__fdiv_rn(g, den), u), tag);
         }
     };
