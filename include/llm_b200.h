@@ -184,7 +184,13 @@ LLMB_API int llmb_set_layers(llmb_model *m, int layers);
  * "decode_trace" 1 makes models
  * opened afterwards record the persistent kernel's phase timeline, read with
  * llmb_peek(m, "trace", ...) (a profiling aid, the counterpart of GPU.Skip,
- * gpu.go:769-784).  Process-wide, like the Go package variables. */
+ * gpu.go:769-784); "wait_limit_us" N (0 = the default of 2 s) limits
+ * every wait of the persistent kernel (a flag poll, a weight slot) to N
+ * microseconds, past which the launch stops with LLMB_ERR_DEVICE; and
+ * "drop_publish" S >= 0 (-1 = off) makes the persistent kernel skip one
+ * publish at decode step S (the step counts prompt tokens too), so that the
+ * next phase's wait runs out (a test aid for that error path, with
+ * wait_limit_us).  Process-wide, like the Go package variables. */
 LLMB_API int llmb_set_knob(const char *name, int64_t value);
 LLMB_API int64_t llmb_get_knob(const char *name);
 
@@ -203,12 +209,18 @@ LLMB_API int64_t llmb_get_knob(const char *name);
  * fixed array in device memory (about 1 MiB, held by every GPU that loads
  * this library until the process exits), so the sizes are limited: at most
  * 32 heads, head_dim 128 and 4096 positions; larger ones return LLMB_ERR_ARG
- * before any work.  The first call on a device looks up the array's address
- * on that device (make it before any stream capture).  Every call shares the
- * array: calls that overlap on the GPU race, so serialise them (one stream).
- * No part of the array needs clearing between calls: a call reads only what
- * it wrote.  Asynchronous on `stream` (a cudaStream_t, NULL for the default
- * stream); the caller synchronises. */
+ * before any work.  Each call made outside stream capture looks up the
+ * array's address on the current device (a host-side query that allocates
+ * nothing), so the address always belongs to the current context; a call made
+ * while `stream` is capturing a graph reuses the address its device's last
+ * call outside capture found, so the first call on a device must come before
+ * any capture.  An error already pending on the calling thread
+ * (cudaPeekAtLastError) makes the call return LLMB_ERR_CUDA without
+ * launching and without clearing it.  Every call shares the array: calls
+ * that overlap on the GPU race, so serialise them (one stream).  No part of
+ * the array needs clearing between calls: a call reads only what it wrote.
+ * Asynchronous on `stream` (a cudaStream_t, NULL for the default stream); the
+ * caller synchronises. */
 LLMB_API int llmb_attention_noalloc(const float *q, const float *k_cache, const float *v_cache, int n_pos, int heads,
                                     int kv_heads, int head_dim, int kv_stride, float *out, void *stream);
 

@@ -101,7 +101,7 @@ def _ptr(a: np.ndarray):
 
 def set_knob(name: str, value: int) -> None:
     """Sets a package knob: decode_batch, prefill_batch, memory_budget, decode_mode, prefill_mode, tag_reset,
-    attn_positions or decode_trace."""
+    attn_positions, decode_trace, wait_limit_us or drop_publish (include/llm_b200.h describes each)."""
     if lib().llmb_set_knob(name.encode(), int(value)) != OK:
         raise LlmError(ERR_ARG, f"llm: no knob {name!r}")
 

@@ -44,7 +44,7 @@ constexpr int kCons = 8;                 // consumer warps
 constexpr int kConsThreads = kCons * 32; // 256
 constexpr int kDecThreads = kConsThreads;  // 8 warps: 2 per SM sub-partition, up to 255 registers each
 constexpr int kFeeder = kConsThreads - 1;  // the thread that issues the weight ring's copies
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: the default limit of every wait
 #ifndef LLMB_POLL_SLEEP_NS
 #define LLMB_POLL_SLEEP_NS 0
 #endif
@@ -130,6 +130,10 @@ __device__ __forceinline__ void ll_put(uint64_t *p, float v, uint32_t tag) {
 
 __device__ __forceinline__ int read_err(const int *e) { return *(volatile const int *)e; }
 
+// The limit of every wait of this launch, in ns (DecParams::wait_ns, or
+// kWaitNs), set once by thread 0 before the first barrier.
+__shared__ uint64_t s_wait_ns;
+
 // A tagged vector to poll into shared memory: src[0, n) (n even), tag, dst.
 struct Seg {
     const uint64_t *src;
@@ -195,7 +199,7 @@ __device__ __noinline__ bool poll_segs(const Seg (&sg)[NS], int *err) {
                 if (kPollSleepNs) __nanosleep(kPollSleepNs);
                 if ((++spins & 255) == 0) {
                     if (read_err(err)) return false;
-                    if (gtimer() - t0 > kWaitNs) {
+                    if (gtimer() - t0 > s_wait_ns) {
                         atomicExch(err, DEV_TAG_TIMEOUT);
                         return false;
                     }
@@ -540,7 +544,7 @@ __device__ __noinline__ float poll_stage(const uint64_t *src, int n, uint32_t ta
             }
             if (pend && (++spins & 255) == 0) {
                 if (read_err(err)) return -1.f;
-                if (gtimer() - t0 > kWaitNs) {
+                if (gtimer() - t0 > s_wait_ns) {
                     atomicExch(err, DEV_TAG_TIMEOUT);
                     return -1.f;
                 }
@@ -592,7 +596,7 @@ __device__ __noinline__ bool poll_stage_res(const uint64_t *src0, int n0, uint32
             }
             if (pend && (++spins & 255) == 0) {
                 if (read_err(err)) return false;
-                if (gtimer() - t0 > kWaitNs) {
+                if (gtimer() - t0 > s_wait_ns) {
                     atomicExch(err, DEV_TAG_TIMEOUT);
                     return false;
                 }
@@ -657,7 +661,7 @@ __device__ __forceinline__ bool slot_wait(uint64_t *full, int sl, unsigned ph, i
             ok = false;
             break;
         }
-        if (gtimer() - t0 > kWaitNs) {
+        if (gtimer() - t0 > s_wait_ns) {
             atomicExch(err, DEV_RING_TIMEOUT);
             ok = false;
             break;
@@ -884,7 +888,7 @@ __device__ void feed_drain(const DecSmem &sm, int nslots, unsigned consumed) {
     for (unsigned v = consumed; v < sm.feed->issued; ++v) {
         const uint64_t t0 = gtimer();
         while (!mbar_try_wait(sm.full + v % nslots, (v / nslots) & 1))
-            if (gtimer() - t0 > kWaitNs / 4) break;
+            if (gtimer() - t0 > s_wait_ns / 4) break;
     }
 }
 
@@ -1263,7 +1267,7 @@ __device__ bool ph_attn_r64(const DecParams &dm, int l, const Tok &tk, int item,
                             ok = false;
                             break;
                         }
-                        if (gtimer() - t0 > kWaitNs) {
+                        if (gtimer() - t0 > s_wait_ns) {
                             atomicExch(dm.err, DEV_TAG_TIMEOUT);
                             ok = false;
                             break;
@@ -1352,7 +1356,8 @@ __device__ bool ph_o(const DecParams &dm, int l, const Tok &tk, const DecSmem &s
     for (int t = s.a; t < s.b; t += s.per) {
         const int k = min(s.per, s.b - t);
         if (!unit_rows(dm, L.o, k, sm, rg, t == s.a)) return false;
-        if (threadIdx.x < k * 8) {
+        // (drop_step: a test aid that makes the next phase's wait run out)
+        if (threadIdx.x < k * 8 && !(tk.step == dm.drop_step && l == 0 && blockIdx.x == 0)) {
             const int row = t * 8 + threadIdx.x;
             ll_put(dm.ll_x + row, __fadd_rn(sm.gate[row - s.a * 8], sm.rows[threadIdx.x]), tag);
         }
@@ -1495,7 +1500,7 @@ __device__ __forceinline__ bool head_unit(const DecParams &dm, int k, int t0, fl
                 ok = false;
                 break;
             }
-            if (gtimer() - t0w > kWaitNs) {
+            if (gtimer() - t0w > s_wait_ns) {
                 atomicExch(dm.err, DEV_RING_TIMEOUT);
                 ok = false;
                 break;
@@ -1748,6 +1753,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     for (int j = threadIdx.x; j < nplan; j += kConsThreads)
         sm.plan[j] = dm.feed_plan[(size_t)blockIdx.x * kMaxFeedPlan + j];
     if (threadIdx.x == 0) {
+        s_wait_ns = dm.wait_ns ? dm.wait_ns : kWaitNs;
         for (int i = 0; i < nslots; ++i) mbar_init(sm.full + i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         *sm.feed = Feed{0, 0, 0, 0, 0u, 0, nplan, (unsigned)(ntok * nplan), 0};

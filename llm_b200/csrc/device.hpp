@@ -125,6 +125,14 @@ struct ModelHeader {
     // the token's argmax exchange.  Recorded for the first token of a launch.
     uint64_t *trace;
     int trace_events;
+    // the persistent decode kernel's limit on every wait (flag polls, weight
+    // slots), in ns; 0 means the default of 2 s.  Past it the kernel records
+    // DEV_TAG_TIMEOUT or DEV_RING_TIMEOUT in err and returns.
+    uint64_t wait_ns;
+    // a test aid for that error path: at the token whose step (state[1]) is
+    // drop_step, CTA 0 does not publish its output-projection rows of layer
+    // 0, so the gate/up phase's wait for them runs out.  -1: off.
+    int drop_step;
 };
 
 

@@ -38,6 +38,8 @@ std::atomic<int64_t> g_decode_trace{0};  // 1: record the persistent kernel's ph
 std::atomic<int64_t> g_prefill_mode{0};   // 0: chunked products (gemm.cu), 1: the per-token kernels
 std::atomic<int64_t> g_tag_reset{0};      // > 0: reset the decode kernel's tags after that many tokens (a test aid)
 std::atomic<int64_t> g_attn_positions{0}; // positions per attention item of the decode kernel (0: as many as fit)
+std::atomic<int64_t> g_wait_limit_us{0};  // the decode kernel's limit on each wait, microseconds (0: 2 s)
+std::atomic<int64_t> g_drop_publish{-1};  // a test aid: the step at which the decode kernel skips one publish
 
 thread_local std::string t_open_error;
 
@@ -473,6 +475,12 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
 
 // ------------------------------------------------------------- running --
 
+cudaError_t reset_tags(Model &m);
+
+// Reads the device error word (after everything queued on the stream).  On an
+// error it is cleared, and so are the persistent kernel's tagged buffers: a
+// launch that gave up leaves words whose tags the next launch would reuse
+// (the epoch counter advances only when a launch completes).
 Error check_device(Model &m) {
     CUDA_TRY(cudaMemcpyAsync(m.h_err, m.hdm.err, 4, cudaMemcpyDeviceToHost, m.st));
     CUDA_TRY(cudaStreamSynchronize(m.st));
@@ -480,6 +488,8 @@ Error check_device(Model &m) {
         const int e = *m.h_err;
         *m.h_err = 0;
         cudaMemsetAsync(m.hdm.err, 0, 4, m.st);
+        reset_tags(m);
+        m.ll_tokens = 0;
         cudaStreamSynchronize(m.st);
         const char *what = e == DEV_BARRIER_TIMEOUT ? "a grid barrier of the decode kernel timed out"
                            : e == DEV_TAG_TIMEOUT   ? "an activation of the decode kernel did not arrive in time"
@@ -586,6 +596,8 @@ Error decode(Model &m, int cnt) {
             CUDA_TRY(reset_tags(m));
             m.ll_tokens = 0;
         }
+        m.dp->wait_ns = (uint64_t)g_wait_limit_us.load() * 1000u;
+        m.dp->drop_step = (int)g_drop_publish.load();
         CUDA_TRY(launch_decode2(*m.dp, m.dec, cnt, m.persistent_ctas, m.st));
         m.ll_tokens += cnt;
         m.stats.dispatches++;
@@ -1070,6 +1082,8 @@ int llmb_set_knob(const char *name, int64_t v) {
     else if (s == "prefill_mode") g_prefill_mode = v ? 1 : 0;
     else if (s == "tag_reset") g_tag_reset = v > 0 ? v : 0;
     else if (s == "attn_positions") g_attn_positions = v > 0 ? std::clamp<int64_t>(v, 64, 256) / 32 * 32 : 0;
+    else if (s == "wait_limit_us") g_wait_limit_us = std::clamp<int64_t>(v, 0, 10000000);
+    else if (s == "drop_publish") g_drop_publish = v >= 0 ? std::min<int64_t>(v, INT32_MAX) : -1;
     else return LLMB_ERR_ARG;
     return LLMB_OK;
 }
@@ -1085,6 +1099,8 @@ int64_t llmb_get_knob(const char *name) {
     if (s == "prefill_mode") return g_prefill_mode;
     if (s == "tag_reset") return g_tag_reset;
     if (s == "attn_positions") return g_attn_positions;
+    if (s == "wait_limit_us") return g_wait_limit_us;
+    if (s == "drop_publish") return g_drop_publish;
     return -1;
 }
 

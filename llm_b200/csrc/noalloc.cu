@@ -87,7 +87,12 @@ __global__ void __launch_bounds__(kNaThreads) k_na_merge(int n, int hd, const fl
     }
 }
 
-// The scratch's device address, per device, found once (with that device current).
+// The scratch's device address per device.  Outside stream capture every
+// call looks it up again with that device current (cudaGetSymbolAddress is a
+// host-side query; it allocates nothing), so an address never outlives the
+// context it belongs to (a cudaDeviceReset, or another context made current
+// on the device, gets a fresh one).  A call made while its stream captures a
+// graph uses the address its device's last call outside capture found.
 std::mutex g_mu;
 float *g_addr[64];
 
@@ -104,23 +109,31 @@ extern "C" LLMB_API int llmb_attention_noalloc(const float *q, const float *k_ca
         return LLMB_ERR_ARG;
     if (heads > kNaMaxHeads || head_dim > kNaMaxHeadDim || n_pos > kNaMaxChunks * kNaChunk)
         return LLMB_ERR_ARG;  // beyond the fixed scratch: at most 32 heads, head_dim 128, 4096 positions
+    // An error left pending by earlier work is the caller's: report it without
+    // clearing it and without launching.
+    if (cudaPeekAtLastError() != cudaSuccess) return LLMB_ERR_CUDA;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LLMB_ERR_CUDA;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return LLMB_ERR_CUDA;
     float *scratch;
     {
         std::lock_guard<std::mutex> lock(g_mu);
-        if (!g_addr[dev]) {
+        if (cap == cudaStreamCaptureStatusNone) {
             void *p = nullptr;
             if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || !p) return LLMB_ERR_CUDA;
             g_addr[dev] = static_cast<float *>(p);
+        } else if (!g_addr[dev]) {
+            return LLMB_ERR_CUDA;  // the first call on a device must come before any capture
         }
         scratch = g_addr[dev];
     }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int nch = (n_pos + kNaChunk - 1) / kNaChunk;
     const float scale = (float)(1.0 / std::sqrt((double)head_dim));  // cpu.go:304
     k_na_partial<<<dim3(nch, heads), kNaThreads, 0, st>>>(q, k_cache, v_cache, n_pos, heads, kv_heads, head_dim,
                                                           kv_stride, scale, scratch);
+    if (cudaGetLastError() != cudaSuccess) return LLMB_ERR_CUDA;  // this launch's own error (none was pending)
     k_na_merge<<<heads, kNaThreads, 0, st>>>(n_pos, head_dim, scratch, out);
     return cudaGetLastError() == cudaSuccess ? LLMB_OK : LLMB_ERR_CUDA;
 }

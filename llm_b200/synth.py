@@ -48,6 +48,12 @@ class Spec:
     emb_type: int = T_Q4_0
     out_type: int | None = None  # None: tied output (token_embd is the head)
     types: dict = field(default_factory=dict)  # per matrix kind, default Q4_0
+    # Rows of the output matrix written as copies of others, so that logits tie
+    # exactly at every step: "far" copies row i to row i + vocab/2 (tiles far
+    # apart, so different CTAs of the head), "near" copies row 2i to 2i + 1
+    # (the same 8-row tile).  The argmax must return the lower index
+    # (kernels.go:351-353, cpu.go:389-397).
+    tie: str = ""
 
     def mtype(self, kind: str) -> int:
         return self.types.get(kind, T_Q4_0)
@@ -71,7 +77,12 @@ TINY_QWEN = Spec("tiny-qwen2", 13, "qwen2", 384, 3, 6, 2, 768, 1536, 1e6, 1e-6, 
 # head_dim 128 (the other supported head size)
 TINY_HD128 = Spec("tiny-hd128", 14, "llama", 512, 2, 4, 2, 1024, 1024, 1e4, 1e-5)
 
-SPECS = {s.name: s for s in (C1, C2, C3, TINY_LLAMA, TINY_MIXED, TINY_QWEN, TINY_HD128)}
+# Every logit has an exact twin (untied Q4_0 / Q8_0 output): the greedy tie rule on the GPU.
+TINY_TIE_FAR = Spec("tiny-tie-far", 15, "llama", 256, 3, 4, 2, 512, 1024, 1e4, 1e-5, out_type=T_Q4_0, tie="far")
+TINY_TIE_NEAR = Spec("tiny-tie-near", 16, "llama", 256, 3, 4, 2, 512, 1024, 1e4, 1e-5, out_type=T_Q8_0, tie="near")
+
+SPECS = {s.name: s for s in (C1, C2, C3, TINY_LLAMA, TINY_MIXED, TINY_QWEN, TINY_HD128, TINY_TIE_FAR,
+                              TINY_TIE_NEAR)}
 
 # The five BASELINE.json configurations: which file, prompt length, greedy tokens, context.
 WORKLOADS = {
@@ -86,6 +97,23 @@ WORKLOADS = {
 def prompt_ids(vocab: int, n: int, seed: int) -> np.ndarray:
     """Uniform-random token ids (the benchmark prompts), seeded."""
     return np.random.default_rng(1000 + seed).integers(0, vocab, n, dtype=np.int64).astype(np.int32)
+
+
+def workload_prompts(k: int, rank: int = 0) -> list[np.ndarray]:
+    """The prompts of BASELINE workload k as the benchmark runs them.
+
+    Workloads 1-4: one prompt of the workload's length, ids uniform over the
+    vocab, seeded by the model's seed. Workload 5: the streams of one GPU
+    (rank), lengths uniform on the prompt range and ids uniform, seeded per
+    rank and per stream."""
+    w = WORKLOADS[k]
+    s = w["spec"]
+    if k != 5:
+        return [prompt_ids(s.vocab, w["prompt"], seed=s.seed)]
+    rng = np.random.default_rng(5000 + rank)
+    lo, hi = w["prompt_range"]
+    lens = rng.integers(lo, hi + 1, w["streams"])
+    return [prompt_ids(s.vocab, int(n), seed=10000 * (rank + 1) + i) for i, n in enumerate(lens)]
 
 
 def _blocks(rng: np.random.Generator, ty: int, rows: int, cols: int) -> np.ndarray:
@@ -195,6 +223,12 @@ def write(s: Spec, path: str) -> None:
                     f.write(v.astype("<f4").tobytes())
                 else:
                     blk = _blocks(rng, ty, dims[1], dims[0])
+                    if name == "output.weight" and s.tie:
+                        rows = blk.reshape(dims[1], -1)
+                        if s.tie == "far":
+                            rows[dims[1] // 2:] = rows[: dims[1] // 2]
+                        else:
+                            rows[1::2] = rows[0::2]
                     assert blk.size == size
                     f.write(blk.tobytes())
             end = len(hdr) + infos[-1][3] + infos[-1][4]

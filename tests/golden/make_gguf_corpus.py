@@ -64,4 +64,6 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_gguf_corpus.py REFERENCE_CHECKOUT")
+    main(sys.argv[1])
