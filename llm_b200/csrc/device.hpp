@@ -150,6 +150,15 @@ using DevModel = ModelDesc<kMaxLayers>;
 using DecParams = ModelDesc<kMaxDecLayers>;
 static_assert(sizeof(DecParams) < 32000, "kernel parameters are limited to 32 KB");
 
+// CTAs of the persistent decode kernel that take QKV rows (T tiles): the
+// first ones, leaving the last `heads` CTAs, which take the attention items of
+// a token's first context chunk, free to start their items (their K/V loads)
+// while the QKV rows are computed.
+__host__ __device__ inline int dec_qkv_ctas(int T, int ncta, int heads) {
+    const int p = ncta - heads > ncta / 2 ? ncta - heads : ncta;
+    return T < p ? T : p;
+}
+
 // Shared-memory layout of the persistent decode kernel (byte offsets).
 struct DecLayout {
     size_t ring, full, feed, plan, lay, shares, xv, xq8, xs, part, rows, gate, red, att, merge, pre, kvs, nrm, total;
@@ -171,7 +180,7 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     l.xv = p, p += vec;
     l.xq8 = p, p += vec;
     l.xs = p, p += vec;
-    l.part = p, p += 8 * 64;
+    l.part = p, p += 4 * 8 * 64;  // float partials [up to 8 tiles][8 rows][8 warps]
     l.rows = p, p += 4 * 256;
     l.gate = p, p += 4 * (size_t)gate_rows;
     // an attention item's history K rows [dec_chunk][head_dim + 4] and V rows

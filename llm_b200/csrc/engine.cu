@@ -409,7 +409,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
         const int max_tile = max_tile_of(d, c.layers);
         const int T = F / 8, P = std::min(m.persistent_ctas, T);
         d.dec_gate_rows = (T + P - 1) / P * 8;
-        const int Tq = (E + 2 * kvd) / 8, Pq = std::min(m.persistent_ctas, Tq);
+        const int Tq = (E + 2 * kvd) / 8, Pq = dec_qkv_ctas(Tq, m.persistent_ctas, c.heads);
         d.dec_qkv_rows = (Tq + Pq - 1) / Pq * 8;
         // the output and down shares reuse the gate buffer for their residual rows
         const int To = E / 8, Po = std::min(m.persistent_ctas, To);

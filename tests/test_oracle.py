@@ -271,3 +271,17 @@ def test_trace_max_layers(oracle, model_path):
     ref = NumpyModel(path, 8)
     assert np.allclose(x0, ref.w["token_embd.weight"][7], rtol=0, atol=1e-7)
     assert cpu.pos == 1
+
+
+@pytest.mark.parametrize("spec", ["tiny-tie-far", "tiny-tie-near"])
+def test_tie_models_tie_every_step(oracle, model_path, spec):
+    """The tie models (an output matrix of identical row pairs) give every logit an exact twin in the oracle,
+    and its greedy tokens are always the lower index of the pair (cpu.go:389-397)."""
+    from llm_b200 import synth
+
+    s = synth.SPECS[spec]
+    cpu = oracle.CPU(model_path(spec), 256)
+    toks, lg = cpu.generate(synth.prompt_ids(s.vocab, 12, seed=3), 16, step_logits=True)
+    a, b = (lg[:, : s.vocab // 2], lg[:, s.vocab // 2:]) if s.tie == "far" else (lg[:, 0::2], lg[:, 1::2])
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert np.all(toks < s.vocab // 2) if s.tie == "far" else np.all(toks % 2 == 0)
