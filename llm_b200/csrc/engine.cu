@@ -35,7 +35,8 @@ std::atomic<int64_t> g_prefill_batch{kMaxPrefill};
 std::atomic<int64_t> g_memory_budget{0};
 std::atomic<int64_t> g_decode_mode{0};  // 0: persistent kernel, 1: per-phase kernels
 std::atomic<int64_t> g_decode_trace{0};  // 1: record the persistent kernel's phase timeline (llmb_peek "trace")
-std::atomic<int64_t> g_prefill_mode{0};   // 0: chunked products (gemm.cu), 1: the per-token kernels
+std::atomic<int64_t> g_prefill_mode{0};   // 0: chunked products on the tensor cores, 1: the per-token kernels,
+                                          // 2: chunked products in float32 on the CUDA cores (gemm.cu)
 std::atomic<int64_t> g_tag_reset{0};      // > 0: reset the decode kernel's tags after that many tokens (a test aid)
 std::atomic<int64_t> g_attn_positions{0}; // positions per attention item of the decode kernel (0: as many as fit)
 std::atomic<int64_t> g_wait_limit_us{0};  // the decode kernel's limit on each wait, microseconds (0: 2 s)
@@ -318,6 +319,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     s.head_ctas = std::max(1, std::min(nsm * 2, (s.head_tiles + kWarps - 1) / kWarps));
     d.smem_vec = smem_vec_floats(s);
     CUDA_TRY(prepare_kernels(s));
+    CUDA_TRY(prepare_products());
     m.persistent_ctas = nsm;
 
     Error err{LLMB_OK, ""};
@@ -494,6 +496,7 @@ Error check_device(Model &m) {
         const char *what = e == DEV_BARRIER_TIMEOUT ? "a grid barrier of the decode kernel timed out"
                            : e == DEV_TAG_TIMEOUT   ? "an activation of the decode kernel did not arrive in time"
                            : e == DEV_RING_TIMEOUT  ? "a weight slot of the decode kernel timed out"
+                           : e == DEV_MMA_TIMEOUT   ? "a tensor-core product did not complete in time"
                                                     : "a token past the context";
         return {LLMB_ERR_DEVICE, std::string("llm: ") + what};
     }
@@ -518,14 +521,15 @@ Error begin(Model &m, const int32_t *prompt, int n) {
 // as a CUDA graph captured on first use (the kernels read positions, tokens
 // and KV slots from device memory, so one graph serves every call).
 Error run_layers_mm(Model &m, int cnt, int nl, const TokBatch *tb) {
-    const int64_t key = ((int64_t)cnt * 2 + (tb ? 1 : 0)) * 1024 + nl;
+    const bool tensor = g_prefill_mode.load() == 0;
+    const int64_t key = (((int64_t)cnt * 2 + (tb ? 1 : 0)) * 1024 + nl) * 2 + (tensor ? 1 : 0);
     auto it = m.graphs.find(key);
     if (it == m.graphs.end()) {
         CUDA_TRY(cudaStreamBeginCapture(m.st, cudaStreamCaptureModeThreadLocal));
         launch_embed(m.dm, m.sh, cnt, m.st, tb);
         cudaError_t e = cudaGetLastError();
         for (int l = 0; l < nl && e == cudaSuccess; l++)
-            e = launch_layer_mm(m.dm, m.hdm, m.sh, l, cnt, m.persistent_ctas, m.st, tb);
+            e = launch_layer_mm(m.dm, m.hdm, m.sh, l, cnt, m.persistent_ctas, m.st, tb, tensor);
         cudaGraph_t g = nullptr;
         const cudaError_t e2 = cudaStreamEndCapture(m.st, &g);
         if (e == cudaSuccess) e = e2;
@@ -547,7 +551,7 @@ Error prefill(Model &m, int n) {
     for (int a = 0; a < n; a += m.pm) {
         const int cnt = std::min(m.pm, n - a);
         const bool last = a + cnt == n;
-        if (g_prefill_mode.load() == 0) {
+        if (g_prefill_mode.load() != 1) {
             Error e = run_layers_mm(m, cnt, nl, nullptr);
             if (e.code) return e;
             m.stats.dispatches += 1 + 7 * nl;
@@ -759,7 +763,7 @@ Error ensure_batch(Model &m, int nseq) {
 // and returns the head's tokens in m.h_tb->out.
 Error run_batch(Model &m, int cnt, int nh) {
     CUDA_TRY(cudaMemcpyAsync(m.tb, m.h_tb, sizeof(TokBatch), cudaMemcpyHostToDevice, m.st));
-    const bool mm = g_prefill_mode.load() == 0;
+    const bool mm = g_prefill_mode.load() != 1;
     if (mm) {
         Error e = run_layers_mm(m, cnt, m.cfg.layers, m.tb);
         if (e.code) return e;
@@ -769,7 +773,9 @@ Error run_batch(Model &m, int cnt, int nh) {
         m.stats.dispatches += 5 * m.cfg.layers;
     }
     if (nh > 0) {
-        if (mm) CUDA_TRY(launch_head_mm(m.dm, m.hdm, m.sh, m.tb, m.tb->head_rows, nh, m.persistent_ctas, m.st));
+        if (mm)
+            CUDA_TRY(launch_head_mm(m.dm, m.hdm, m.sh, m.tb, m.tb->head_rows, nh, m.persistent_ctas, m.st,
+                                    g_prefill_mode.load() == 0));
         else launch_head_batch(m.dm, m.sh, m.tb, nh, m.st);
         m.stats.dispatches += mm ? 3 : 1;
         CUDA_TRY(cudaMemcpyAsync(m.h_tb->out, m.tb->out, (size_t)nh * 4, cudaMemcpyDeviceToHost, m.st));
@@ -1079,7 +1085,7 @@ int llmb_set_knob(const char *name, int64_t v) {
     else if (s == "memory_budget") g_memory_budget = std::max<int64_t>(v, 0);
     else if (s == "decode_mode") g_decode_mode = v ? 1 : 0;
     else if (s == "decode_trace") g_decode_trace = v ? 1 : 0;
-    else if (s == "prefill_mode") g_prefill_mode = v ? 1 : 0;
+    else if (s == "prefill_mode") g_prefill_mode = std::clamp<int64_t>(v, 0, 2);
     else if (s == "tag_reset") g_tag_reset = v > 0 ? v : 0;
     else if (s == "attn_positions") g_attn_positions = v > 0 ? std::clamp<int64_t>(v, 64, 256) / 32 * 32 : 0;
     else if (s == "wait_limit_us") g_wait_limit_us = std::clamp<int64_t>(v, 0, 10000000);

@@ -21,12 +21,14 @@
 // SwiGLU, or per-token argmax partials for the vocabulary head.  The next
 // K block's loads are issued before the current block's products.
 #include <cooperative_groups.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cfloat>
 #include <cstdint>
 #include <initializer_list>
+#include <utility>
 
 #include "kernels.hpp"
 
@@ -40,6 +42,7 @@ constexpr int kTM = 64;    // tokens per CTA tile
 constexpr int kTR = 64;    // weight rows per CTA tile (8 tiles of 8 rows)
 constexpr int kXS = kTM + 4;  // shared row stride (floats) of the k-major staging arrays
 constexpr int kGT = 256;   // threads
+constexpr unsigned kFull = 0xffffffffu;
 
 __device__ __forceinline__ float b2f(uint32_t v, int k) {
     return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | k));
@@ -402,6 +405,449 @@ __global__ void __launch_bounds__(kGT) k_argmax_rows(const DevModel *__restrict_
     }
 }
 
+// ------------------------------------------------ tensor-core products --
+// The same products on the 5th-generation tensor cores (tcgen05), exact to
+// float32 level by error-compensated splitting.  A CTA owns 128 weight rows x
+// 64 tokens (the MMA's M x N) and a share of K (the cluster split and the
+// distributed-shared-memory reduction of k_gemm).  Per 32-wide K block:
+//   - the weights are dequantised exactly in float32 (d * (q - 8) of Q4_0 has
+//     at most 15 significant bits, d * q of Q8_0 18; Q4_1's d * q + m is the
+//     float32 result) and split into bf16 pieces a = a1 + a2 (+ a3), each the
+//     bf16 rounding of what the earlier pieces leave: exact for Q4_0 with two
+//     pieces, and to float32 with three;
+//   - the activations are split the same way into three bf16 pieces
+//     x = x1 + x2 + x3 (exact for every float32);
+//   - tcgen05.mma (kind::f16, bf16 x bf16 -> f32 in tensor memory) adds the
+//     piece products a1 x1, a1 x2, a2 x1, a1 x3, a2 x2 (and a3 x1): every
+//     product of two bf16 pieces is exact, and the dropped ones are below
+//     2^-24 of a x (|a2|, |x2| <= 2^-9, |a3|, |x3| <= 2^-17 relative).
+// The operands are written by all threads into shared memory in the MMA's
+// K-major canonical layout without swizzle (8-row x 16-byte core matrices),
+// two stages deep, so one block's split overlaps the previous block's MMAs;
+// one thread issues the MMAs and tcgen05.commit signals an mbarrier when they
+// have read a stage.  The accumulator (128 lanes x 64 columns of f32 per
+// matrix) is read back with tcgen05.ld and goes through k_gemm's epilogues.
+namespace tc {
+
+constexpr int kMR = 128;                   // weight rows per CTA (MMA M)
+constexpr int kMN = 64;                    // tokens per CTA (MMA N; rows of X past m are zero)
+constexpr int kAPiece = kMR * 32 * 2;      // one bf16 piece of a 128 x 32 weight block (8 KB)
+constexpr int kBPiece = kMN * 32 * 2;      // one bf16 piece of a 64 x 32 activation block (4 KB)
+constexpr int kPartLd = kMR + 4;           // floats per token of the accumulator copy in shared memory
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s: the limit of a wait for the tensor cores
+
+__host__ __device__ constexpr int stage_bytes(int na) { return na * 3 * kAPiece + 3 * kBPiece; }
+__host__ __device__ constexpr int part_bytes(int na) { return na * kMN * kPartLd * 4; }
+__host__ __device__ constexpr int smem_bytes(int na) {
+    return (2 * stage_bytes(na) > part_bytes(na) ? 2 * stage_bytes(na) : part_bytes(na)) + 64;
+}
+
+// Byte offset of element (row, k) of a K-major canonical operand with `groups`
+// 8-row groups: core matrix (row / 8, k / 8) at ((k / 8) * groups + row / 8) * 128,
+// rows 16 bytes apart inside it.  So the stride between 8-row groups (SBO) is
+// 128 bytes and between 8-element K chunks (LBO) groups * 128.
+__device__ __forceinline__ uint32_t cm_off(int row, int kc, int groups) {
+    return (uint32_t)((kc * groups + (row >> 3)) * 128 + (row & 7) * 16);
+}
+
+// Shared-memory matrix descriptor (SWIZZLE_NONE, version 1 for sm_100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor: kind::f16 with bf16 A and B, f32 D, both K-major, M = 128, N = 64.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kMN >> 3) << 17) |
+                            ((uint32_t)(kMR >> 4) << 24);
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
+            tmem_d),
+        "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool bar_try(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(su32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t gtime() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits (bounded) for phase `parity` of an mbarrier; false after the limit (or
+// once another CTA has recorded an error).
+__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t parity, int *err) {
+    if (bar_try(bar, parity)) return true;
+    const uint64_t t0 = gtime();
+    unsigned spins = 0;
+    while (!bar_try(bar, parity)) {
+        if ((++spins & 63) == 0) {
+            if (*(volatile int *)err) return false;
+            if (gtime() - t0 > kWaitNs) {
+                atomicExch(err, DEV_MMA_TIMEOUT);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Two floats into three bf16 pieces each (packed pairs, first value in the low half).
+__device__ __forceinline__ void split3(float v0, float v1, uint32_t &p1, uint32_t &p2, uint32_t &p3) {
+    const __nv_bfloat162 h1 = __floats2bfloat162_rn(v0, v1);
+    const float2 f1 = __bfloat1622float2(h1);
+    const float r0 = v0 - f1.x, r1 = v1 - f1.y;  // exact
+    const __nv_bfloat162 h2 = __floats2bfloat162_rn(r0, r1);
+    const float2 f2 = __bfloat1622float2(h2);
+    const __nv_bfloat162 h3 = __floats2bfloat162_rn(r0 - f2.x, r1 - f2.y);
+    p1 = *reinterpret_cast<const uint32_t *>(&h1);
+    p2 = *reinterpret_cast<const uint32_t *>(&h2);
+    p3 = *reinterpret_cast<const uint32_t *>(&h3);
+}
+
+// Eight values (one core-matrix row) split and stored into pieces 0..NP-1 (piece stride `pstride` bytes).
+template <int NP>
+__device__ __forceinline__ void store_split8(uint8_t *base, uint32_t off, int pstride, const float (&v)[8]) {
+    uint32_t p[3][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (NP == 3) {
+            split3(v[2 * i], v[2 * i + 1], p[0][i], p[1][i], p[2][i]);
+        } else {
+            const __nv_bfloat162 h1 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            const float2 f1 = __bfloat1622float2(h1);
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i] - f1.x, v[2 * i + 1] - f1.y);
+            p[0][i] = *reinterpret_cast<const uint32_t *>(&h1);
+            p[1][i] = *reinterpret_cast<const uint32_t *>(&h2);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < NP; ++j) *reinterpret_cast<uint4 *>(base + j * pstride + off) = make_uint4(p[j][0], p[j][1], p[j][2], p[j][3]);
+}
+
+// A thread's raw share of one weight block (loaded a block ahead of its use):
+// row t / 2, half t % 2 of its quants (Q4: bytes 8h..8h+7; Q8_0: bytes
+// 16h..16h+15), its scale and (Q4_1) minimum.
+struct ARaw {
+    uint4 w;
+    float d, mn;
+    int type;  // 0: no row (past the matrices)
+};
+
+__device__ __forceinline__ void load_a(const MatSet &ms, int total, int r0, int kb, ARaw &R) {
+    const int row = threadIdx.x >> 1, h = threadIdx.x & 1;
+    R.type = 0;
+    if (r0 + row >= total) return;
+    int lr = 0;
+    const QMat &m = ms.m[mat_of(ms, r0 + row, lr)];
+    const uint8_t *tile = m.tiles + (size_t)(lr >> 3) * m.tile_bytes;
+    const int r = lr & 7;
+    R.type = m.type;
+    if (m.type == 8) {
+        R.w = __ldg(reinterpret_cast<const uint4 *>(tile + ((size_t)kb * 8 + r) * 32 + 16 * h));
+        R.d = __half2float(__ldg(reinterpret_cast<const __half *>(tile + (size_t)m.nb * 256) + kb * 8 + r));
+    } else {
+        const uint2 w = __ldg(reinterpret_cast<const uint2 *>(tile + ((size_t)kb * 8 + r) * 16 + 8 * h));
+        R.w = make_uint4(w.x, w.y, 0u, 0u);
+        const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)m.nb * 128);
+        R.d = __half2float(__ldg(dp + kb * 8 + r));
+        if (m.type == 3) R.mn = __half2float(__ldg(dp + (size_t)m.nb * 8 + kb * 8 + r));
+    }
+}
+
+// The raw share dequantised exactly in float32 and split into the NP bf16
+// pieces of the A operand at a (Q4: elements 8h.. -> chunk h and 16+8h.. ->
+// chunk 2+h; Q8_0: 16h.. -> chunk 2h and 16h+8.. -> chunk 2h+1).  A missing
+// row is zero.
+template <int NP>
+__device__ __forceinline__ void stage_a(const ARaw &R, uint8_t *a) {
+    const int row = threadIdx.x >> 1, h = threadIdx.x & 1;
+    float lo[8], hi[8];
+    if (R.type == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) lo[i] = hi[i] = 0.f;
+    } else if (R.type == 8) {
+        const uint32_t u[4] = {R.w.x ^ 0x80808080u, R.w.y ^ 0x80808080u, R.w.z ^ 0x80808080u, R.w.w ^ 0x80808080u};
+        constexpr float off = 8388736.f;  // 2^23 + 128
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            lo[i] = R.d * (b2f(u[0], i) - off), lo[4 + i] = R.d * (b2f(u[1], i) - off);
+            hi[i] = R.d * (b2f(u[2], i) - off), hi[4 + i] = R.d * (b2f(u[3], i) - off);
+        }
+    } else {
+        const uint32_t l0 = R.w.x & 0x0F0F0F0Fu, l1 = R.w.y & 0x0F0F0F0Fu;
+        const uint32_t h0 = (R.w.x >> 4) & 0x0F0F0F0Fu, h1 = (R.w.y >> 4) & 0x0F0F0F0Fu;
+        if (R.type == 3) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                lo[i] = fmaf(R.d, b2f(l0, i) - 8388608.f, R.mn), lo[4 + i] = fmaf(R.d, b2f(l1, i) - 8388608.f, R.mn);
+                hi[i] = fmaf(R.d, b2f(h0, i) - 8388608.f, R.mn), hi[4 + i] = fmaf(R.d, b2f(h1, i) - 8388608.f, R.mn);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                lo[i] = R.d * (b2f(l0, i) - 8388616.f), lo[4 + i] = R.d * (b2f(l1, i) - 8388616.f);
+                hi[i] = R.d * (b2f(h0, i) - 8388616.f), hi[4 + i] = R.d * (b2f(h1, i) - 8388616.f);
+            }
+        }
+    }
+    const bool q8 = R.type == 8;
+    store_split8<NP>(a, cm_off(row, q8 ? 2 * h : h, kMR / 8), kAPiece, lo);
+    store_split8<NP>(a, cm_off(row, q8 ? 2 * h + 1 : 2 + h, kMR / 8), kAPiece, hi);
+}
+
+// A thread's share of one activation block: token t / 4, columns 8 (t % 4)..+7.
+__device__ __forceinline__ void load_b(const float *x, int K, int m, int kb, float4 &u, float4 &w) {
+    const int tok = threadIdx.x >> 2, c = threadIdx.x & 3;
+    u = w = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tok < m) {
+        const float4 *p = reinterpret_cast<const float4 *>(x + (size_t)tok * K + kb * 32 + 8 * c);
+        u = __ldcg(p), w = __ldcg(p + 1);
+    }
+}
+
+__device__ __forceinline__ void stage_b(const float4 &u, const float4 &w, uint8_t *b) {
+    const int tok = threadIdx.x >> 2, c = threadIdx.x & 3;
+    const float v[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+    store_split8<3>(b, cm_off(tok, c, kMN / 8), kBPiece, v);
+}
+
+#define TC_LD32(taddr, r)                                                                                          \
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, " \
+                 "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, " \
+                 "[%32];"                                                                                          \
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), \
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),       \
+                   "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),     \
+                   "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),     \
+                   "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                                                          \
+                 : "r"(taddr))
+
+}  // namespace tc
+
+// grid (row tiles of 128, splits), cluster (1, splits, 1); 9 warps.  NM
+// matrices (2: gate and up) share the activations; each has its own
+// accumulator (64 tensor-memory columns).  Warps 0-7 stage the operands of
+// each K block (two stages deep) and signal `full`; warp 8 allocates the
+// tensor memory, waits for `full`, issues the block's MMAs from one thread
+// and commits them to `empty`, which releases the stage.  No block-wide
+// barrier separates K blocks, so staging overlaps the tensor cores.
+constexpr int kMT = kGT + 32;  // threads of k_mma: 8 staging warps and the MMA warp
+
+template <int EPI>
+__global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs ga) {
+    using namespace tc;
+    constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
+    constexpr int kCols = 64 * NM;  // tensor-memory columns (a power of 2, >= 32)
+    extern __shared__ __align__(1024) uint8_t tsm[];
+    __shared__ uint32_t tmem_slot;
+    uint64_t *full = reinterpret_cast<uint64_t *>(tsm + smem_bytes(NM) - 64);  // [2]: a stage is staged
+    uint64_t *empty = full + 2;                                                // [2]: its MMAs have read it
+    const DevModel &dm = *ga.dm;
+    const int rt = blockIdx.x, sp = blockIdx.y, r0 = rt * kMR;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool mma_warp = warp == kGT / 32;
+    const int kb0 = ga.nb * sp / ga.splits, kb1 = ga.nb * (sp + 1) / ga.splits;
+    const int K = ga.nb * 32, nblk = kb1 - kb0;
+    // bf16 pieces of the weights: two when every matrix is Q4_0 (exact), else three
+    int np = 2;
+    for (int i = 0; i < ga.a.nm; ++i) np = ga.a.m[i].type != 2 ? 3 : np;
+    for (int i = 0; i < (NM == 2 ? ga.b.nm : 0); ++i) np = ga.b.m[i].type != 2 ? 3 : np;
+    if (mma_warp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_slot)),
+                     "r"(kCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(full + i)), "r"(kGT / 32));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(empty + i)));
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+    if (!mma_warp) {
+        int tot[2] = {0, 0};
+        for (int i = 0; i < ga.a.nm; ++i) tot[0] += ga.a.m[i].rows;
+        for (int i = 0; i < (NM == 2 ? ga.b.nm : 0); ++i) tot[1] += ga.b.m[i].rows;
+        // Block i's raw operands are loaded during block i - 1 into the other of two register sets (two
+        // blocks per pass, so that no set is copied: a copy would wait for the loads).
+        ARaw ra[2][NM];
+        float4 xu[2], xw[2];
+        if (nblk > 0) {
+            for (int j = 0; j < NM; ++j) load_a(j == 0 ? ga.a : ga.b, tot[j], r0, kb0, ra[0][j]);
+            load_b(ga.x, K, ga.m, kb0, xu[0], xw[0]);
+        }
+        auto step = [&](int i, int cur) {
+            const int st = i & 1;
+            uint8_t *stage = tsm + st * stage_bytes(NM);
+            if (i + 1 < nblk) {
+                for (int j = 0; j < NM; ++j) load_a(j == 0 ? ga.a : ga.b, tot[j], r0, kb0 + i + 1, ra[cur ^ 1][j]);
+                load_b(ga.x, K, ga.m, kb0 + i + 1, xu[cur ^ 1], xw[cur ^ 1]);
+            }
+            if (i >= 2) {  // the MMAs of block i - 2 have read this stage (one wait per warp)
+                bool w = true;
+                if (lane == 0) w = bar_wait(empty + st, ((i >> 1) - 1) & 1, dm.err);
+                if (!__shfl_sync(kFull, w, 0)) {
+                    ok = false;
+                    return;
+                }
+            }
+            for (int j = 0; j < NM; ++j) {
+                if (np == 3) stage_a<3>(ra[cur][j], stage + j * 3 * kAPiece);
+                else stage_a<2>(ra[cur][j], stage + j * 3 * kAPiece);
+            }
+            stage_b(xu[cur], xw[cur], stage + NM * 3 * kAPiece);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the operands, to the tensor cores' proxy
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(full + st)) : "memory");
+        };
+        for (int i = 0; i < nblk && ok; i += 2) {
+            step(i, 0);
+            if (ok && i + 1 < nblk) step(i + 1, 1);
+        }
+    } else if (lane == 0) {
+        // descriptors of stage 0, piece 0, K step 0 (the others are byte offsets added to the address field)
+        const uint64_t da0 = sdesc(su32(tsm), (kMR / 8) * 128, 128);
+        const uint64_t db0 = sdesc(su32(tsm + NM * 3 * kAPiece), (kMN / 8) * 128, 128);
+        constexpr uint64_t pa[6] = {0, 0, 1, 0, 1, 2}, pb[6] = {0, 1, 0, 2, 1, 0};  // exact products down to 2^-18 of a x
+        const int npairs = np == 3 ? 6 : 5;
+        for (int i = 0; i < nblk; ++i) {
+            const int st = i & 1;
+            if (!bar_wait(full + st, (i >> 1) & 1, dm.err)) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint64_t so = (uint64_t)(st * stage_bytes(NM)) >> 4;
+            for (int j = 0; j < NM; ++j)
+#pragma unroll
+                for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+                    for (int q = 0; q < 6; ++q) {
+                        if (q >= npairs) break;
+                        const uint64_t da =
+                            da0 + so + (((uint64_t)j * 3 * kAPiece + pa[q] * kAPiece + ks * 2 * (kMR / 8) * 128) >> 4);
+                        const uint64_t db = db0 + so + ((pb[q] * kBPiece + ks * 2 * (kMN / 8) * 128) >> 4);
+                        mma(tmem + j * 64, da, db, (i > 0 || ks > 0 || q > 0) ? 1u : 0u);
+                    }
+            commit(empty + st);
+        }
+    }
+    // the last block's MMAs (and so all before them) are done
+    if (ok && nblk > 0 && !mma_warp) {
+        bool w = true;
+        if (lane == 0) w = bar_wait(empty + ((nblk - 1) & 1), ((nblk - 1) >> 1) & 1, dm.err);
+        ok = __shfl_sync(kFull, w, 0);
+    }
+    ok = !__syncthreads_or(!ok);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    // accumulators -> part[j][token][row] (token-major, so that 4 consecutive rows of a token are one float4;
+    // the stages are free): warp w < 8 reads lanes 32 (w % 4).. of columns 32 (w / 4)..
+    float *part = reinterpret_cast<float *>(tsm);
+    if (ok && !mma_warp) {
+        const int row = 32 * (warp & 3) + lane, c0 = 32 * (warp >> 2);
+        for (int j = 0; j < NM; ++j) {
+            uint32_t r[32];
+            if (nblk > 0) {
+                TC_LD32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + j * 64 + c0, r);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) r[c] = 0u;
+            }
+            float *pr = part + ((size_t)j * kMN + c0) * kPartLd + row;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) pr[c * kPartLd] = __uint_as_float(r[c]);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (mma_warp) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+    if (EPI == EPI_ARGMAX) {  // no split: the tile's best row per token
+        __shared__ float bvs[4][kMN];
+        __shared__ int bis[4][kMN];
+        if (!mma_warp) {
+            const int t = threadIdx.x & 63, seg = threadIdx.x >> 6;
+            float bv = -FLT_MAX;
+            int bi = 0x7fffffff;
+            for (int rr = seg * 32; ok && rr < seg * 32 + 32; ++rr) {
+                const int row = r0 + rr;
+                const float v = part[(size_t)t * kPartLd + rr];
+                if (row < dm.vocab && better(v, row, bv, bi)) bv = v, bi = row;
+            }
+            bvs[seg][t] = bv, bis[seg][t] = bi;
+        }
+        __syncthreads();
+        if (ok && threadIdx.x < ga.m) {
+            float v = bvs[0][threadIdx.x];
+            int ix = bis[0][threadIdx.x];
+            for (int q = 1; q < 4; ++q)
+                if (better(bvs[q][threadIdx.x], bis[q][threadIdx.x], v, ix)) v = bvs[q][threadIdx.x], ix = bis[q][threadIdx.x];
+            dm.gam[(size_t)threadIdx.x * gridDim.x + rt] = make_float2(v, __int_as_float(ix));
+        }
+    } else {
+        // the cluster's partials summed in rank order, then the epilogue: work item (4-row group u, token t)
+        cg::cluster_group cl = cg::this_cluster();
+        if (ga.splits > 1) cl.sync();
+        const int S = ga.splits;
+        // items token-major (t = it / 32, u = it % 32), CTA sp taking a contiguous share, so that a warp's
+        // threads cover consecutive 4-row groups of one token (coalesced epilogue stores)
+        const int items = (kMR / 4) * ga.m, i0 = items * sp / S, i1 = items * (sp + 1) / S;
+        int total = 0;
+        for (int i = 0; i < ga.a.nm; ++i) total += ga.a.m[i].rows;
+        for (int it = i0 + (int)threadIdx.x; ok && !mma_warp && it < i1; it += kGT) {
+            const int t = it >> 5, u = it & 31;
+            const int g = r0 + 4 * u;
+            if (g >= total) continue;
+            // every rank's float4 of rows 4u..4u+3 at token t loaded first, then summed in rank order
+            float4 pv[8][NM];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                if (r < S) {
+                    const float *rs = S > 1 ? cl.map_shared_rank(part, r) : part;
+#pragma unroll
+                    for (int j = 0; j < NM; ++j)
+                        pv[r][j] = *reinterpret_cast<const float4 *>(rs + ((size_t)j * kMN + t) * kPartLd + 4 * u);
+                }
+            }
+            float v[NM][4];
+#pragma unroll
+            for (int j = 0; j < NM; ++j) {
+                v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    if (r < S) v[j][0] += pv[r][j].x, v[j][1] += pv[r][j].y, v[j][2] += pv[r][j].z, v[j][3] += pv[r][j].w;
+            }
+            int la = 0;
+            const int seg = mat_of(ga.a, g, la);
+            epilogue<EPI, NM>(ga, dm, ga.a.m[seg], seg, la, g, t, 0, v);
+        }
+        if (ga.splits > 1) cl.sync();  // the partials stay readable until every CTA of the cluster is done
+    }
+}
+
 MatSet mats(std::initializer_list<const QMat *> ms) {
     MatSet s{};
     for (const QMat *m : ms) s.m[s.nm++] = *m;
@@ -433,10 +879,46 @@ cudaError_t gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, k_gemm<EPI>, ga);
 }
 
+template <int EPI>
+cudaError_t mma_gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st) {
+    constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
+    GemmArgs ga = base;
+    const int row_tiles = (rows + tc::kMR - 1) / tc::kMR;
+    ga.splits = EPI == EPI_ARGMAX ? 1 : splits_for(row_tiles, ga.nb, nsm);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(row_tiles, ga.splits);
+    cfg.blockDim = dim3(kMT);
+    cfg.dynamicSmemBytes = tc::smem_bytes(NM);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = ga.splits, attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_mma<EPI>, ga);
+}
+
+template <int EPI>
+cudaError_t product(bool tensor, const GemmArgs &ga, int rows, int nsm, cudaStream_t st) {
+    return tensor ? mma_gemm<EPI>(ga, rows, nsm, st) : gemm<EPI>(ga, rows, nsm, st);
+}
+
 }  // namespace
 
+cudaError_t prepare_products() {
+    const std::pair<const void *, int> fs[] = {{(const void *)k_mma<EPI_QKV>, tc::smem_bytes(1)},
+                                               {(const void *)k_mma<EPI_RESID>, tc::smem_bytes(1)},
+                                               {(const void *)k_mma<EPI_SWIGLU>, tc::smem_bytes(2)},
+                                               {(const void *)k_mma<EPI_ARGMAX>, tc::smem_bytes(1)}};
+    for (const auto &f : fs) {
+        const cudaError_t e = cudaFuncSetAttribute(f.first, cudaFuncAttributeMaxDynamicSharedMemorySize, f.second);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 cudaError_t launch_layer_mm(const DevModel *dm, const DevModel &hd, const Shapes &s, int l, int m, int nsm,
-                            cudaStream_t st, const TokBatch *tb) {
+                            cudaStream_t st, const TokBatch *tb, bool tensor) {
     const Layer &L = hd.layer[l];
     const int E = s.embd, F = s.ff;
     GemmArgs ga{};
@@ -444,29 +926,30 @@ cudaError_t launch_layer_mm(const DevModel *dm, const DevModel &hd, const Shapes
     // QKV
     k_norm_rows<<<m, kGT, 0, st>>>(dm, L.attn_norm, nullptr, 0);
     ga.x = hd.h, ga.nb = E / 32, ga.a = mats({&L.q, &L.k, &L.v});
-    cudaError_t e = gemm<EPI_QKV>(ga, L.q.rows + L.k.rows + L.v.rows, nsm, st);
+    cudaError_t e = product<EPI_QKV>(tensor, ga, L.q.rows + L.k.rows + L.v.rows, nsm, st);
     // attention (per token, per head and chunk of 64 positions)
     launch_attention(dm, s, l, m, st, tb);
     // x += Wo att
     ga.x = hd.att, ga.nb = E / 32, ga.a = mats({&L.o}), ga.out = hd.x, ga.out_ld = E;
-    if (e == cudaSuccess) e = gemm<EPI_RESID>(ga, L.o.rows, nsm, st);
+    if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.o.rows, nsm, st);
     // act = SwiGLU(Wgate h, Wup h)
     k_norm_rows<<<m, kGT, 0, st>>>(dm, L.ffn_norm, nullptr, 0);
     ga.x = hd.h, ga.nb = E / 32, ga.a = mats({&L.gate}), ga.b = mats({&L.up}), ga.out = hd.act, ga.out_ld = F;
-    if (e == cudaSuccess) e = gemm<EPI_SWIGLU>(ga, L.gate.rows, nsm, st);
+    if (e == cudaSuccess) e = product<EPI_SWIGLU>(tensor, ga, L.gate.rows, nsm, st);
     // x += Wdown act
     ga.x = hd.act, ga.nb = F / 32, ga.a = mats({&L.down}), ga.b = MatSet{}, ga.out = hd.x, ga.out_ld = E;
-    if (e == cudaSuccess) e = gemm<EPI_RESID>(ga, L.down.rows, nsm, st);
+    if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.down.rows, nsm, st);
     return e;
 }
 
 cudaError_t launch_head_mm(const DevModel *dm, const DevModel &hd, const Shapes &s, TokBatch *tb, const int *rows_dev,
-                           int rows, int nsm, cudaStream_t st) {
+                           int rows, int nsm, cudaStream_t st, bool tensor) {
     k_norm_rows<<<rows, kGT, 0, st>>>(dm, hd.out_norm, rows_dev, 0);
     GemmArgs ga{};
     ga.dm = dm, ga.tb = tb, ga.m = rows, ga.x = hd.h, ga.nb = s.embd / 32, ga.a = mats({&hd.head});
-    const cudaError_t e = gemm<EPI_ARGMAX>(ga, hd.head.rows, nsm, st);
-    k_argmax_rows<<<rows, kGT, 0, st>>>(dm, tb, (hd.head.rows + kTR - 1) / kTR);
+    const cudaError_t e = product<EPI_ARGMAX>(tensor, ga, hd.head.rows, nsm, st);
+    const int tile_rows = tensor ? tc::kMR : kTR;
+    k_argmax_rows<<<rows, kGT, 0, st>>>(dm, tb, (hd.head.rows + tile_rows - 1) / tile_rows);
     return e;
 }
 

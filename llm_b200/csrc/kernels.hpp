@@ -14,6 +14,7 @@ enum DeviceError : int {
     DEV_CONTEXT_FULL = 2,     // a token past the context
     DEV_TAG_TIMEOUT = 3,      // a tagged activation did not arrive in time
     DEV_RING_TIMEOUT = 4,     // a weight slot did not fill or drain in time
+    DEV_MMA_TIMEOUT = 5,      // the tensor cores did not signal a product's completion in time
 };
 
 // Host copy of what launch shapes need.
@@ -60,13 +61,17 @@ void launch_attention(const DevModel *dm, const Shapes &s, int l, int m, cudaStr
 // One layer for m <= 64 tokens through the chunked products of gemm.cu
 // (norm, QKV product with bias/RoPE/KV append, attention, output product +
 // residual, norm, gate/up product + SwiGLU, down product + residual); hd is
-// the host copy of *dm (device pointers), nsm the SMs to fill.
+// the host copy of *dm (device pointers), nsm the SMs to fill.  tensor: the
+// products on the tensor cores (k_mma, split bf16 pieces), else in float32 on
+// the CUDA cores (k_gemm).
 cudaError_t launch_layer_mm(const DevModel *dm, const DevModel &hd, const Shapes &s, int l, int m, int nsm,
-                            cudaStream_t st, const TokBatch *tb);
+                            cudaStream_t st, const TokBatch *tb, bool tensor);
 // The head for `rows` residual rows listed at rows_dev (device): final norm,
 // the vocabulary product and the argmax of each row into tb->out.
 cudaError_t launch_head_mm(const DevModel *dm, const DevModel &hd, const Shapes &s, TokBatch *tb, const int *rows_dev,
-                           int rows, int nsm, cudaStream_t st);
+                           int rows, int nsm, cudaStream_t st, bool tensor);
+// Lets the tensor-core products use their dynamic shared memory (once per device).
+cudaError_t prepare_products();
 
 // The argmax of the residual rows tb->head_rows[0..rows) into tb->out.
 void launch_head_batch(const DevModel *dm, const Shapes &s, TokBatch *tb, int rows, cudaStream_t st);
