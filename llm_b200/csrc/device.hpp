@@ -25,6 +25,7 @@ constexpr int kMaxLayers = 256;
 constexpr int kAttnChunk = 64;     // positions per attention partial (flash-decoding split)
 constexpr int kMaxPrefill = 64;    // tokens per prefill chunk (PrefillBatch, gpu.go:165)
 constexpr int kMaxDecodeBatch = 16; // MaxBatch, gpu.go:1046
+constexpr int kSsqTiles = 8;       // 128-row tiles of a residual row (embd <= 1024)
 
 struct QMat {
     const uint8_t *tiles = nullptr;  // tile t at tiles + t * tile_bytes
@@ -103,6 +104,9 @@ struct ModelHeader {
     // head's per (token, row tile) argmax partials
     float *h;
     float2 *gam;
+    // the tensor-core products' RMSNorm inputs: per token, the sums of squares of the residual row over
+    // each 128-row tile ([kMaxPrefill][kSsqTiles], written by the embedding and the residual epilogues)
+    float *ssq;
 
     // the persistent decode kernel's tagged activations ({f32 value, u32 tag})
     uint64_t *ll_x, *ll_q, *ll_k, *ll_v, *ll_att, *ll_act, *ll_pv, *ll_ml;

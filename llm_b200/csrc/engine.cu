@@ -389,6 +389,7 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     if (!(d.tokens = m.alloc<int32_t>((size_t)(ctx + 1) * 4, err))) return err;
     if (!(d.am_part = m.alloc<float2>((size_t)head_parts * kMaxPrefill * 8, err))) return err;
     if (!(d.h = m.alloc<float>((size_t)pm * E * 4, err))) return err;
+    if (!(d.ssq = m.alloc<float>((size_t)pm * kSsqTiles * 4, err))) return err;
     if (!(d.gam = m.alloc<float2>((size_t)pm * ((d.head.rows + 63) / 64) * 8, err))) return err;
     if (!(d.am_count = m.alloc<uint32_t>(kMaxPrefill * 4, err))) return err;
     if (!(d.err = m.alloc<int>(4, err))) return err;
@@ -554,7 +555,7 @@ Error prefill(Model &m, int n) {
         if (g_prefill_mode.load() != 1) {
             Error e = run_layers_mm(m, cnt, nl, nullptr);
             if (e.code) return e;
-            m.stats.dispatches += 1 + 7 * nl;
+            m.stats.dispatches += 1 + (g_prefill_mode.load() == 0 ? 5 : 7) * nl;
         } else {
             if (nl == 0) {
                 launch_embed(m.dm, m.sh, cnt, m.st);
@@ -767,7 +768,7 @@ Error run_batch(Model &m, int cnt, int nh) {
     if (mm) {
         Error e = run_layers_mm(m, cnt, m.cfg.layers, m.tb);
         if (e.code) return e;
-        m.stats.dispatches += 1 + 7 * m.cfg.layers;
+        m.stats.dispatches += 1 + (g_prefill_mode.load() == 0 ? 5 : 7) * m.cfg.layers;
     } else {
         for (int l = 0; l < m.cfg.layers; l++) launch_layer(m.dm, m.sh, l, cnt, m.st, m.tb);
         m.stats.dispatches += 5 * m.cfg.layers;

@@ -152,6 +152,11 @@ struct GemmArgs {
     int l;               // layer (QKV: which KV cache)
     float *out;          // RESID: x [m][E]; SWIGLU: act [m][F]
     int out_ld;
+    // k_mma only: with norm_w, x is the raw residual and the product reads RMSNorm(x) * norm_w per token
+    // (cpu.go:81-98), the norm taken from the rows' sums of squares in dm.ssq; a RESID product also
+    // writes its output rows' sums of squares there (with ssq_out set)
+    const float *norm_w;
+    bool ssq_out;
 };
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
@@ -613,19 +618,31 @@ __device__ __forceinline__ void stage_a(const ARaw &R, uint8_t *a) {
     store_split8<NP>(a, cm_off(row, q8 ? 2 * h + 1 : 2 + h, kMR / 8), kAPiece, hi);
 }
 
-// A thread's share of one activation block: token t / 4, columns 8 (t % 4)..+7.
-__device__ __forceinline__ void load_b(const float *x, int K, int m, int kb, float4 &u, float4 &w) {
+// A thread's share of one activation block: token t / 4, columns 8 (t % 4)..+7
+// (and, with a norm, the 8 norm weights of those columns).
+__device__ __forceinline__ void load_b(const float *x, const float *nw, int K, int m, int kb, float4 (&u)[4]) {
     const int tok = threadIdx.x >> 2, c = threadIdx.x & 3;
-    u = w = make_float4(0.f, 0.f, 0.f, 0.f);
+    u[0] = u[1] = u[2] = u[3] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (tok < m) {
         const float4 *p = reinterpret_cast<const float4 *>(x + (size_t)tok * K + kb * 32 + 8 * c);
-        u = __ldcg(p), w = __ldcg(p + 1);
+        u[0] = __ldcg(p), u[1] = __ldcg(p + 1);
+        if (nw) {
+            const float4 *q = reinterpret_cast<const float4 *>(nw + kb * 32 + 8 * c);
+            u[2] = __ldg(q), u[3] = __ldg(q + 1);
+        }
     }
 }
 
-__device__ __forceinline__ void stage_b(const float4 &u, const float4 &w, uint8_t *b) {
+// The block into the three B pieces; with a norm, each value is (x * s) * w
+// first (cpu.go:94-97's rounding points), s the token's 1 / rms.
+__device__ __forceinline__ void stage_b(const float4 (&u)[4], bool norm, float s, uint8_t *b) {
     const int tok = threadIdx.x >> 2, c = threadIdx.x & 3;
-    const float v[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+    float v[8] = {u[0].x, u[0].y, u[0].z, u[0].w, u[1].x, u[1].y, u[1].z, u[1].w};
+    if (norm) {
+        const float w[8] = {u[2].x, u[2].y, u[2].z, u[2].w, u[3].x, u[3].y, u[3].z, u[3].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], s), w[i]);
+    }
     store_split8<3>(b, cm_off(tok, c, kMN / 8), kBPiece, v);
 }
 
@@ -675,6 +692,7 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
                      "r"(kCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    __shared__ float s_norm[kMN];
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(full + i)), "r"(kGT / 32));
@@ -694,17 +712,32 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
         // Block i's raw operands are loaded during block i - 1 into the other of two register sets (two
         // blocks per pass, so that no set is copied: a copy would wait for the loads).
         ARaw ra[2][NM];
-        float4 xu[2], xw[2];
+        float4 xb[2][4];
+        const bool norm = ga.norm_w != nullptr;
         if (nblk > 0) {
             for (int j = 0; j < NM; ++j) load_a(j == 0 ? ga.a : ga.b, tot[j], r0, kb0, ra[0][j]);
-            load_b(ga.x, K, ga.m, kb0, xu[0], xw[0]);
+            load_b(ga.x, ga.norm_w, K, ga.m, kb0, xb[0]);
+        }
+        // RMSNorm scale of each token (cpu.go:81-98: 1 / sqrt(mean of squares + eps) in double, rounded
+        // to float), from the row's sums of squares per 128-row tile, added in tile order; read while the
+        // first block's operands load, then shared by the staging warps (named barrier 1)
+        float sn = 1.f;
+        if (norm) {
+            if ((int)threadIdx.x < ga.m) {
+                const int ntiles = (ga.nb * 32 + kMR - 1) / kMR;
+                float ss = 0.f;
+                for (int i = 0; i < ntiles; ++i) ss += __ldcg(dm.ssq + (size_t)threadIdx.x * kSsqTiles + i);
+                s_norm[threadIdx.x] = (float)(1.0 / sqrt((double)__fadd_rn(__fdiv_rn(ss, (float)(ga.nb * 32)), dm.eps)));
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kGT) : "memory");
+            if ((int)(threadIdx.x >> 2) < ga.m) sn = s_norm[threadIdx.x >> 2];
         }
         auto step = [&](int i, int cur) {
             const int st = i & 1;
             uint8_t *stage = tsm + st * stage_bytes(NM);
             if (i + 1 < nblk) {
                 for (int j = 0; j < NM; ++j) load_a(j == 0 ? ga.a : ga.b, tot[j], r0, kb0 + i + 1, ra[cur ^ 1][j]);
-                load_b(ga.x, K, ga.m, kb0 + i + 1, xu[cur ^ 1], xw[cur ^ 1]);
+                load_b(ga.x, ga.norm_w, K, ga.m, kb0 + i + 1, xb[cur ^ 1]);
             }
             if (i >= 2) {  // the MMAs of block i - 2 have read this stage (one wait per warp)
                 bool w = true;
@@ -718,7 +751,7 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
                 if (np == 3) stage_a<3>(ra[cur][j], stage + j * 3 * kAPiece);
                 else stage_a<2>(ra[cur][j], stage + j * 3 * kAPiece);
             }
-            stage_b(xu[cur], xw[cur], stage + NM * 3 * kAPiece);
+            stage_b(xb[cur], norm, sn, stage + NM * 3 * kAPiece);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the operands, to the tensor cores' proxy
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(full + st)) : "memory");
@@ -813,13 +846,50 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
         if (ga.splits > 1) cl.sync();
         const int S = ga.splits;
         // items token-major (t = it / 32, u = it % 32), CTA sp taking a contiguous share, so that a warp's
-        // threads cover consecutive 4-row groups of one token (coalesced epilogue stores)
-        const int items = (kMR / 4) * ga.m, i0 = items * sp / S, i1 = items * (sp + 1) / S;
+        // threads cover consecutive 4-row groups of one token (coalesced epilogue stores).  With ssq_out
+        // (a residual product) CTA sp takes whole tokens, a warp per token, so that the warp can sum the
+        // squares of its token's new rows.
+        const int items = (kMR / 4) * ga.m;
+        const bool tok_rows = EPI == EPI_RESID && ga.ssq_out;
+        const int i0 = tok_rows ? 32 * (ga.m * sp / S) : items * sp / S;
+        const int i1 = tok_rows ? 32 * (ga.m * (sp + 1) / S) : items * (sp + 1) / S;
         int total = 0;
         for (int i = 0; i < ga.a.nm; ++i) total += ga.a.m[i].rows;
+        // (with tok_rows i0 is a multiple of 32, so every warp's 32 items are one token's)
         for (int it = i0 + (int)threadIdx.x; ok && !mma_warp && it < i1; it += kGT) {
             const int t = it >> 5, u = it & 31;
             const int g = r0 + 4 * u;
+            if (tok_rows) {
+                // a warp per token: every lane takes part in the sum (rows past the matrix add 0)
+                float sq = 0.f;
+                if (g < total) {
+                    float4 pv[8];
+#pragma unroll
+                    for (int r = 0; r < 8; ++r)
+                        if (r < S) {
+                            const float *rs = S > 1 ? cl.map_shared_rank(part, r) : part;
+                            pv[r] = *reinterpret_cast<const float4 *>(rs + (size_t)t * kPartLd + 4 * u);
+                        }
+                    float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int r = 0; r < 8; ++r)
+                        if (r < S) v[0] += pv[r].x, v[1] += pv[r].y, v[2] += pv[r].z, v[3] += pv[r].w;
+                    int la = 0;
+                    const QMat &ma = ga.a.m[mat_of(ga.a, g, la)];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if (la + c >= ma.rows) continue;
+                        float *p = ga.out + (size_t)t * ga.out_ld + g + c;
+                        const float nv = __fadd_rn(__ldcg(p), v[c]);
+                        *p = nv;
+                        sq = fmaf(nv, nv, sq);
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
+                if (u == 0) dm.ssq[(size_t)t * kSsqTiles + rt] = sq;
+                continue;
+            }
             if (g >= total) continue;
             // every rank's float4 of rows 4u..4u+3 at token t loaded first, then summed in rank order
             float4 pv[8][NM];
@@ -923,19 +993,31 @@ cudaError_t launch_layer_mm(const DevModel *dm, const DevModel &hd, const Shapes
     const int E = s.embd, F = s.ff;
     GemmArgs ga{};
     ga.dm = dm, ga.tb = tb, ga.m = m, ga.l = l;
-    // QKV
-    k_norm_rows<<<m, kGT, 0, st>>>(dm, L.attn_norm, nullptr, 0);
-    ga.x = hd.h, ga.nb = E / 32, ga.a = mats({&L.q, &L.k, &L.v});
+    // QKV (the tensor-core products fold the RMSNorm in; the float32 ones read the normed rows)
+    if (tensor) {
+        ga.x = hd.x, ga.norm_w = L.attn_norm;
+    } else {
+        k_norm_rows<<<m, kGT, 0, st>>>(dm, L.attn_norm, nullptr, 0);
+        ga.x = hd.h;
+    }
+    ga.nb = E / 32, ga.a = mats({&L.q, &L.k, &L.v});
     cudaError_t e = product<EPI_QKV>(tensor, ga, L.q.rows + L.k.rows + L.v.rows, nsm, st);
+    ga.norm_w = nullptr;
     // attention (per token, per head and chunk of 64 positions)
     launch_attention(dm, s, l, m, st, tb);
     // x += Wo att
-    ga.x = hd.att, ga.nb = E / 32, ga.a = mats({&L.o}), ga.out = hd.x, ga.out_ld = E;
+    ga.x = hd.att, ga.nb = E / 32, ga.a = mats({&L.o}), ga.out = hd.x, ga.out_ld = E, ga.ssq_out = tensor;
     if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.o.rows, nsm, st);
     // act = SwiGLU(Wgate h, Wup h)
-    k_norm_rows<<<m, kGT, 0, st>>>(dm, L.ffn_norm, nullptr, 0);
-    ga.x = hd.h, ga.nb = E / 32, ga.a = mats({&L.gate}), ga.b = mats({&L.up}), ga.out = hd.act, ga.out_ld = F;
+    if (tensor) {
+        ga.x = hd.x, ga.norm_w = L.ffn_norm;
+    } else {
+        k_norm_rows<<<m, kGT, 0, st>>>(dm, L.ffn_norm, nullptr, 0);
+        ga.x = hd.h;
+    }
+    ga.nb = E / 32, ga.a = mats({&L.gate}), ga.b = mats({&L.up}), ga.out = hd.act, ga.out_ld = F;
     if (e == cudaSuccess) e = product<EPI_SWIGLU>(tensor, ga, L.gate.rows, nsm, st);
+    ga.norm_w = nullptr;
     // x += Wdown act
     ga.x = hd.act, ga.nb = F / 32, ga.a = mats({&L.down}), ga.b = MatSet{}, ga.out = hd.x, ga.out_ld = E;
     if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.down.rows, nsm, st);

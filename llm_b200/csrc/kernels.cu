@@ -507,11 +507,28 @@ __device__ __forceinline__ Smem smem_views(float *base, const DevModel &dm) { re
 
 // ---------------------------------------------------- per-phase kernels --
 
+// The embedding rows of m tokens into x, and each row's sum of squares into
+// ssq[t][0] (the tensor-core products' RMSNorm input; the other tiles' 0).
 __global__ void __launch_bounds__(kThreads) k_embed(const DevModel *__restrict__ dmp, const TokBatch *tb) {
     const DevModel &dm = *dmp;
     const int t = blockIdx.x;
     const int tok = tb ? tb->tok[t] : dm.tokens[dm.state[1] + t];
-    for (int e = threadIdx.x; e < dm.embd; e += kThreads) dm.x[(size_t)t * dm.embd + e] = gather(dm.embed, tok, e);
+    float ss = 0.f;
+    for (int e = threadIdx.x; e < dm.embd; e += kThreads) {
+        const float v = gather(dm.embed, tok, e);
+        dm.x[(size_t)t * dm.embd + e] = v;
+        ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    __shared__ float red[kWarps];
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < kSsqTiles) {
+        float v = 0.f;
+        if (threadIdx.x == 0)
+            for (int w = 0; w < kWarps; ++w) v += red[w];
+        dm.ssq[(size_t)t * kSsqTiles + threadIdx.x] = v;
+    }
 }
 
 __global__ void __launch_bounds__(kThreads) k_qkv(const DevModel *__restrict__ dmp, int l, const TokBatch *tb) {
