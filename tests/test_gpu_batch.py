@@ -64,12 +64,13 @@ def test_batch_more_sequences_than_a_launch(oracle, gpus):
         assert np.array_equal(got[i], cpu.generate(p, n)), i
 
 
-def test_batch_per_token_kernels(oracle, gpus):
-    """prefill_mode 1: the same batches through the per-token kernels."""
+@pytest.mark.parametrize("mode", [1, 2], ids=["per-token", "fp32-products"])
+def test_batch_other_paths(oracle, gpus, mode):
+    """prefill_mode 1 (the per-token kernels) and 2 (the float32 CUDA-core products): the same batches."""
     g = gpus("tiny-mixed", 256)
     prompts = prompts_for(g.cfg.vocab, [3, 66, 20], seed=80)
     old = llm_b200.get_knob("prefill_mode")
-    llm_b200.set_knob("prefill_mode", 1)
+    llm_b200.set_knob("prefill_mode", mode)
     try:
         got, _ = g.generate_batch(prompts, 12)
     finally:

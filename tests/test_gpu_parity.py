@@ -113,6 +113,29 @@ def test_prefill_per_token_kernels(oracle, gpus, spec):
         assert int(np.argmax(got)) == oracle.argmax(want)
 
 
+@pytest.mark.parametrize("spec", ["tiny-llama", "tiny-mixed", "tiny-qwen2", "tiny-hd128", "c2-smollm2-mixed"])
+@pytest.mark.parametrize("n_prompt", [3, 64, 150])
+def test_prefill_products_tensor_and_fp32(oracle, gpus, spec, n_prompt):
+    """The chunked products on the tensor cores (prefill_mode 0, tcgen05 with split bf16 pieces) and in float32
+    on the CUDA cores (prefill_mode 2): the last prompt token's logits against the oracle, both within 1e-5."""
+    old = llm_b200.get_knob("prefill_mode")
+    g = gpus(spec, 256)
+    prompt = synth.prompt_ids(g.cfg.vocab, n_prompt, seed=n_prompt + 3)
+    got = {}
+    try:
+        for mode in (0, 2):
+            llm_b200.set_knob("prefill_mode", mode)
+            got[mode] = g.prefill_logits(prompt)
+    finally:
+        llm_b200.set_knob("prefill_mode", old)
+    cpu = oracle.CPU(synth.ensure(spec), 256)
+    for t in prompt:
+        want = cpu.forward(int(t))
+    for mode in (0, 2):
+        assert rel_err(got[mode], want) <= REL_TOL, (mode, rel_err(got[mode], want))
+        assert int(np.argmax(got[mode])) == oracle.argmax(want)
+
+
 @pytest.mark.parametrize("spec", ["tiny-llama", "tiny-mixed", "tiny-qwen2"])
 def test_generate_every_step(oracle, gpus, decode_mode, spec):
     """Every decoded step's logits and token against the oracle's greedy run."""
