@@ -318,7 +318,7 @@ struct DecSmem {
     float *xv;               // activation vector, paired layout for Q4 / plain for Q8 (max(E,F) floats)
     float *xq8;              // the same vector in plain layout when a Q8_0 matrix reads it
     float *xs;               // raw residual (E floats)
-    double *part;            // float partial sums [8 tiles of a unit][8 rows][kCons warps]
+    double *part;            // [kCons][8 tiles-in-unit max 8][8 rows] partial sums
     float *rows;             // row results of a unit [64]
     float *gate;             // gate rows of this CTA's gate/up share (max 8 * 64 rows)
     float *red;              // reduction scratch [64]
@@ -700,39 +700,14 @@ __device__ __forceinline__ bool slot_wait(uint64_t *full, int sl, unsigned ph, i
     return ok;
 }
 
-// Partial row sums of a unit of k < 8 tiles: the unit's k * nb
-// tile-blocks, tile-major, are cut into 8 contiguous ranges, one per warp
-// (so with k = 1, 2, 4 a warp covers one piece of one tile, and every warp has
-// work for any k); the warp's partial of row r of tile i goes to
-// part[(i * 8 + r) * kCons + warp] (0 for tiles the range misses).  (Loading
-// each block's activations once for all the unit's tiles instead measured
-// 1.6-3x slower: the per-block latency chain, not shared-memory traffic,
-// bounds these products.)
-__device__ __forceinline__ void tile_partials(const QMat &m, int k, const uint8_t *slot, const DecSmem &sm,
-                                              float *part) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = k * m.nb, g0 = (n * warp) >> 3, g1 = (n * (warp + 1)) >> 3;
-#pragma unroll 1
-    for (int i = 0; i < k; ++i) {
-        const int lo = max(g0, i * m.nb) - i * m.nb, hi = min(g1, (i + 1) * m.nb) - i * m.nb;
-        float a = 0.f;
-        if (lo < hi) {
-            a = dot_tile(m.type, slot + (size_t)i * m.tile_bytes, m.nb, sm, lo, hi, lane);
-            a += __shfl_xor_sync(kFull, a, 1);
-            a += __shfl_xor_sync(kFull, a, 2);
-        }
-        if ((lane & 3) == 0) part[(i * 8 + (lane >> 2)) * kCons + warp] = a;
-    }
-}
-
 // Computes the rows of one unit (k tiles of matrix m) into c.rows[k * 8]
-// (row i of the unit).  All consumer warps take part, every lane as (row r =
-// lane / 4, quarter q = lane % 4) of a tile, so a warp reads each 32-weight
-// block of a tile's 8 rows as 128 (Q8_0: 256) contiguous bytes and each
-// activation value once per quarter (a broadcast to the 8 rows).  With
-// k >= 8 each warp takes whole tiles; with fewer every warp takes a
-// contiguous eighth of the unit's tile-blocks, and the 8 warps' partials
-// meet in shared memory (tile_partials), summed in warp order (deterministic).
+// (row i of the unit).  All consumer warps take part: with k >= 8 each warp
+// takes whole tiles; with k == 1 warp w takes row w, a block per lane;
+// otherwise every tile's blocks are split across the warps, whose partials
+// meet through shared memory and three shuffles, in a fixed order.  (Measured
+// against a split of the unit's tile-blocks into 8 contiguous ranges, which
+// keeps all warps busy for 3 and 5-7 tiles: that was 1-3 % slower on both
+// benchmark shapes.)
 // waited: the caller has waited for the slot and passed a consumer barrier since.
 __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const UnitCtx &c, const int sl,
                                              const unsigned ph, const int slot_bytes, int *err, bool waited) {
@@ -749,13 +724,34 @@ __device__ __forceinline__ bool unit_rows_nl(const QMat &m, const int k, const U
             if ((lane & 3) == 0) c.rows[i * 8 + (lane >> 2)] = a;
         }
         __syncwarp();
+    } else if (k == 1) {
+        // one tile: warp w takes its row w, one block per lane, no partial sums across warps
+        const float a = dot_row(m.type, slot, m.nb, warp, sm, lane);
+        if (lane == 0) c.rows[warp] = a;
     } else {
-        tile_partials(m, k, slot, sm, c.part);
+        const int lg = k == 2 ? 2 : k <= 4 ? 1 : 0;  // parts = kCons / k = 1 << lg (k in 2..7), by shifts
+        const int parts = 1 << lg;
+        const int tile = warp >> lg, part = warp & (parts - 1);
+        float a = 0.f;
+        if (tile < k) {
+            const int b0 = (m.nb * part) >> lg, b1 = (m.nb * (part + 1)) >> lg;
+            a = dot_tile(m.type, slot + (size_t)tile * m.tile_bytes, m.nb, sm, b0, b1, lane);
+        }
+        __syncwarp();
+        a += __shfl_xor_sync(kFull, a, 1);
+        a += __shfl_xor_sync(kFull, a, 2);
+        // partial of (row r, warp w) -> part[r * 8 + w]: the 8 parts of a row are 8 consecutive lanes
+        if ((lane & 3) == 0) c.part[(lane >> 2) * 8 + warp] = a;
         cons_sync();
-        if (threadIdx.x < k * 8) {
-            const float4 *p = reinterpret_cast<const float4 *>(c.part + threadIdx.x * kCons);
-            const float4 u = p[0], v = p[1];
-            c.rows[threadIdx.x] = ((((((u.x + u.y) + u.z) + u.w) + v.x) + v.y) + v.z) + v.w;
+        if (threadIdx.x < 64) {
+            // thread (r, w) = (t / 8, t % 8); warps w = tile * parts + p
+            float v = c.part[threadIdx.x];
+            const int w = threadIdx.x & 7;
+            // sum over p within each tile's group of `parts` consecutive warps
+            if (parts >= 2) v += __shfl_xor_sync(kFull, v, 1);
+            if (parts >= 4) v += __shfl_xor_sync(kFull, v, 2);
+            if (parts >= 8) v += __shfl_xor_sync(kFull, v, 4);
+            if ((w & (parts - 1)) == 0 && (w >> lg) < k) c.rows[(w >> lg) * 8 + (threadIdx.x >> 3)] = v;
         }
     }
     cons_sync();
@@ -1536,7 +1532,7 @@ __device__ __forceinline__ bool head_unit(const DecParams &dm, int k, int t0, fl
                 ok = false;
                 break;
             }
-            if (gtimer() - t0w > s_wait_ns) {
+            if (gtimer() - t0w > kWaitNs) {
                 atomicExch(dm.err, DEV_RING_TIMEOUT);
                 ok = false;
                 break;
@@ -1553,7 +1549,7 @@ __device__ __forceinline__ bool head_unit(const DecParams &dm, int k, int t0, fl
             if (better(v, row, bv, bi)) bv = v, bi = row;
         }
     };
-    if (k >= kCons) {
+    if (2 * k > kCons) {
         for (int i = warp; i < k; i += kCons) {
             float a = dot_tile(m.type, slot + (size_t)i * m.tile_bytes, m.nb, sm, 0, m.nb, lane);
             a += __shfl_xor_sync(kFull, a, 1);
@@ -1561,14 +1557,26 @@ __device__ __forceinline__ bool head_unit(const DecParams &dm, int k, int t0, fl
             if ((lane & 3) == 0) finish(i, lane >> 2, a);
         }
     } else {
-        // the unit's tile-blocks in 8 contiguous ranges, one per warp; partials summed in warp order
+        const int lg = k == 2 ? 2 : k <= 4 ? 1 : 0;  // parts = kCons / k = 1 << lg (k in 2..7), by shifts
+        const int parts = 1 << lg;
+        const int tile = warp >> lg, part = warp & (parts - 1);
+        float a = 0.f;
+        if (tile < k) {
+            const int b0 = (m.nb * part) >> lg, b1 = (m.nb * (part + 1)) >> lg;
+            a = dot_tile(m.type, slot + (size_t)tile * m.tile_bytes, m.nb, sm, b0, b1, lane);
+        }
+        a += __shfl_xor_sync(kFull, a, 1);
+        a += __shfl_xor_sync(kFull, a, 2);
         float *part_s = reinterpret_cast<float *>(sm.part);
-        tile_partials(m, k, slot, sm, part_s);
+        if ((lane & 3) == 0) part_s[(lane >> 2) * 8 + warp] = a;
         cons_sync();
-        if (threadIdx.x < k * 8) {
-            const float4 *p = reinterpret_cast<const float4 *>(part_s + threadIdx.x * kCons);
-            const float4 u = p[0], v = p[1];
-            finish(threadIdx.x >> 3, threadIdx.x & 7, ((((((u.x + u.y) + u.z) + u.w) + v.x) + v.y) + v.z) + v.w);
+        if (threadIdx.x < 64) {
+            float v = part_s[threadIdx.x];
+            const int w = threadIdx.x & 7;
+            if (parts >= 2) v += __shfl_xor_sync(kFull, v, 1);
+            if (parts >= 4) v += __shfl_xor_sync(kFull, v, 2);
+            if (parts >= 8) v += __shfl_xor_sync(kFull, v, 4);
+            if ((w & (parts - 1)) == 0 && (w >> lg) < k) finish(w >> lg, threadIdx.x >> 3, v);
         }
     }
     cons_sync();  // the slot (and the shared partials) are free

@@ -184,7 +184,7 @@ __host__ __device__ inline DecLayout dec_layout(int nslots, int slot_bytes, int 
     l.xv = p, p += vec;
     l.xq8 = p, p += vec;
     l.xs = p, p += vec;
-    l.part = p, p += 4 * 8 * 64;  // float partials [up to 8 tiles][8 rows][8 warps]
+    l.part = p, p += 8 * 64;
     l.rows = p, p += 4 * 256;
     l.gate = p, p += 4 * (size_t)gate_rows;
     // an attention item's history K rows [dec_chunk][head_dim + 4] and V rows
