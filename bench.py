@@ -372,13 +372,13 @@ def fp32_roofline(achieved_tflops):
             "peak_source": "nominal FP32 (148 SMs x 128 lanes x 2 x 1.965 GHz; no measured FP32 peak)"}
 
 
-def run_other_configs(local):
-    """Configs 2-4 once each (after a warm-up run): decode and prefill tok/s by CUDA events, one GPU, tokens
-    against the oracle's fixture, and the decode's HBM roofline (prefill's FP32 roofline)."""
+def run_other_configs(local, ks=(2, 3, 4)):
+    """Configs 2-4 (or those of ks) once each (after a warm-up run): decode and prefill tok/s by CUDA events,
+    one GPU, tokens against the oracle's fixture, and the decode's HBM roofline (prefill's FP32 roofline)."""
     import llm_b200
 
     out = {}
-    for k in (2, 3, 4):
+    for k in ks:
         w = synth.WORKLOADS[k]
         g = llm_b200.GPU(synth.ensure(w["spec"]), ctx=w["ctx"], device=local)
         prompt = synth.workload_prompts(k)[0]
@@ -493,7 +493,18 @@ def main():
     ap.add_argument("--c5-gen", type=int, default=0, help="greedy tokens per config 5 sequence (0: the workload's 128)")
     ap.add_argument("--only-multi-stream", action="store_true",
                     help="run only the config 5 measurement and print its object (a profiling aid)")
+    ap.add_argument("--only-config", type=int, choices=[2, 3, 4], default=0,
+                    help="run only this config's single-stream measurement and print its object (a profiling aid)")
+    ap.add_argument("--knob", action="append", default=[], metavar="NAME=VALUE",
+                    help="set a package knob before any model opens (e.g. decode_mode=1 times the per-phase "
+                         "kernels, prefill_mode=2 the FP32 products)")
     args = ap.parse_args()
+    if args.knob and args.impl == "ours":
+        import llm_b200
+
+        for kv in args.knob:
+            name, _, val = kv.partition("=")
+            llm_b200.set_knob(name, int(val))
     ws, rank, local = dist_setup()
     try:
         if args.impl == "reference":
@@ -505,6 +516,12 @@ def main():
             multi = run_multi_stream(args, ws, rank, local)
             if rank == 0:
                 print(json.dumps({"multi_stream": multi}), flush=True)
+        elif args.only_config:
+            import torch
+
+            torch.cuda.set_device(local)
+            if rank == 0:
+                print(json.dumps({"other_configs": run_other_configs(local, (args.only_config,))}), flush=True)
         else:
             run_ours(args, ws, rank, local)
     finally:

@@ -173,8 +173,10 @@ LLMB_API int llmb_set_layers(llmb_model *m, int layers);
  * read by llmb_open).  One more, with no counterpart in the reference:
  * "decode_mode" 0 (default) decodes with the persistent kernel, 1 with one
  * kernel per phase (an A/B and debugging aid); "prefill_mode" 0 (default)
- * runs prompt chunks and multi-stream batches through the chunked products,
- * 1 through one matvec per token and phase (the same aid); "tag_reset" N > 0
+ * runs prompt chunks and multi-stream batches through the chunked products
+ * on the tensor cores (tcgen05, operands split exactly into bf16 pieces,
+ * f32 accumulation), 1 through one matvec per token and phase, 2 through
+ * chunked products on the FP32 CUDA cores (both A/B aids); "tag_reset" N > 0
  * clears the persistent kernel's tagged exchange buffers after every N
  * decoded tokens (a test aid: they are cleared anyway before the 32-bit tags
  * would wrap); "attn_positions" N (64..256, a multiple of 32; read by

@@ -28,6 +28,7 @@
 #include <cfloat>
 #include <cstdint>
 #include <initializer_list>
+#include <mutex>
 #include <utility>
 
 #include "kernels.hpp"
@@ -441,11 +442,23 @@ constexpr int kBPiece = kMN * 32 * 2;      // one bf16 piece of a 64 x 32 activa
 constexpr int kPartLd = kMR + 4;           // floats per token of the accumulator copy in shared memory
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s: the limit of a wait for the tensor cores
 
+constexpr int kDepth = 4;                  // K blocks of raw operands in flight per staging thread (cp.async)
+constexpr int kNwFloats = 1024;            // norm weights of the CTA's K range (a normed product has K = embd <= 1024)
+
+// Shared memory: two stages of bf16 operands (the accumulators' copy for the
+// epilogue aliases them), then kDepth stages of raw operands, then the norm
+// weights, then the mbarriers.  A raw stage holds, per staging thread, the
+// quant bytes (16 B) and the scale / minimum words (8 B) of its row share for
+// each matrix, then its 32 activation bytes (two 16-byte halves).
 __host__ __device__ constexpr int stage_bytes(int na) { return na * 3 * kAPiece + 3 * kBPiece; }
+__host__ __device__ constexpr int raw_bytes(int na) { return na * kGT * 24 + kGT * 32; }
+__host__ __device__ constexpr int raw_off(int na) { return 2 * stage_bytes(na); }
+__host__ __device__ constexpr int nw_off(int na) { return raw_off(na) + kDepth * raw_bytes(na); }
 __host__ __device__ constexpr int part_bytes(int na) { return na * kMN * kPartLd * 4; }
 __host__ __device__ constexpr int smem_bytes(int na) {
-    return (2 * stage_bytes(na) > part_bytes(na) ? 2 * stage_bytes(na) : part_bytes(na)) + 64;
+    return (nw_off(na) + kNwFloats * 4 > part_bytes(na) ? nw_off(na) + kNwFloats * 4 : part_bytes(na)) + 64;
 }
+static_assert(smem_bytes(2) + 4096 <= 232448, "the products' shared memory exceeds the per-block maximum");
 
 // Byte offset of element (row, k) of a K-major canonical operand with `groups`
 // 8-row groups: core matrix (row / 8, k / 8) at ((k / 8) * groups + row / 8) * 128,
@@ -547,34 +560,97 @@ __device__ __forceinline__ void store_split8(uint8_t *base, uint32_t off, int ps
     for (int j = 0; j < NP; ++j) *reinterpret_cast<uint4 *>(base + j * pstride + off) = make_uint4(p[j][0], p[j][1], p[j][2], p[j][3]);
 }
 
-// A thread's raw share of one weight block (loaded a block ahead of its use):
-// row t / 2, half t % 2 of its quants (Q4: bytes 8h..8h+7; Q8_0: bytes
-// 16h..16h+15), its scale and (Q4_1) minimum.
+// A thread's raw share of one weight block: row t / 2, half t % 2 of its
+// quants (Q4: bytes 8h..8h+7; Q8_0: bytes 16h..16h+15), its scale and (Q4_1)
+// minimum.
 struct ARaw {
     uint4 w;
     float d, mn;
     int type;  // 0: no row (past the matrices)
 };
 
-__device__ __forceinline__ void load_a(const MatSet &ms, int total, int r0, int kb, ARaw &R) {
+// Where a thread's raw share of block kb of one matrix lives: the quant bytes
+// at q + kb * qstep, and the 4-byte word holding the scales of its row pair at
+// d + kb * 16 (its own in the high half when hi), the minima mstep bytes after.
+// The thread's row is the same for every block, so this is set up once.
+struct ASrc {
+    const uint8_t *q, *d;
+    int type, hi, qstep, mstep;
+};
+
+__device__ __forceinline__ void a_src(const MatSet &ms, int total, int r0, ASrc &s) {
     const int row = threadIdx.x >> 1, h = threadIdx.x & 1;
-    R.type = 0;
+    s.q = s.d = nullptr;
+    s.type = s.hi = s.qstep = s.mstep = 0;
     if (r0 + row >= total) return;
     int lr = 0;
     const QMat &m = ms.m[mat_of(ms, r0 + row, lr)];
     const uint8_t *tile = m.tiles + (size_t)(lr >> 3) * m.tile_bytes;
     const int r = lr & 7;
-    R.type = m.type;
-    if (m.type == 8) {
-        R.w = __ldg(reinterpret_cast<const uint4 *>(tile + ((size_t)kb * 8 + r) * 32 + 16 * h));
-        R.d = __half2float(__ldg(reinterpret_cast<const __half *>(tile + (size_t)m.nb * 256) + kb * 8 + r));
-    } else {
-        const uint2 w = __ldg(reinterpret_cast<const uint2 *>(tile + ((size_t)kb * 8 + r) * 16 + 8 * h));
-        R.w = make_uint4(w.x, w.y, 0u, 0u);
-        const __half *dp = reinterpret_cast<const __half *>(tile + (size_t)m.nb * 128);
-        R.d = __half2float(__ldg(dp + kb * 8 + r));
-        if (m.type == 3) R.mn = __half2float(__ldg(dp + (size_t)m.nb * 8 + kb * 8 + r));
+    const bool q8 = m.type == 8;
+    s.type = m.type;
+    s.hi = r & 1;
+    s.qstep = q8 ? 256 : 128;
+    s.q = tile + r * (q8 ? 32 : 16) + h * (q8 ? 16 : 8);
+    s.d = tile + (size_t)m.nb * s.qstep + (r & ~1) * 2;
+    s.mstep = m.nb * 16;
+}
+
+__device__ __forceinline__ void cp4(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp8(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+// 16 bytes, of which the first n (0 or 16) are read and the rest zero-filled
+__device__ __forceinline__ void cp16(uint32_t dst, const void *src, uint32_t n = 16) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// This thread's raw operands of block kb into the raw stage at shared address
+// raw: its weight shares (as[j]) and its 8 activations (token t / 4, columns
+// 8 (t % 4)..+7; zeros for tokens past m).
+template <int NM>
+__device__ __forceinline__ void copy_raw(const ASrc (&as)[NM], const float *x, int K, int m, int kb, uint32_t raw) {
+    const int t = threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < NM; ++j) {
+        const ASrc &s = as[j];
+        if (!s.type) continue;
+        const uint32_t aq = raw + (j * kGT + t) * 16, ad = raw + NM * kGT * 16 + (j * kGT + t) * 8;
+        const uint8_t *q = s.q + (size_t)kb * s.qstep, *d = s.d + (size_t)kb * 16;
+        if (s.type == 8) cp16(aq, q);
+        else cp8(aq, q);
+        cp4(ad, d);
+        if (s.type == 3) cp4(ad + 4, d + s.mstep);
     }
+    const int tok = t >> 2, c = t & 3;
+    const bool v = tok < m;
+    const float *p = v ? x + (size_t)tok * K + kb * 32 + 8 * c : x;
+    const uint32_t bx = raw + NM * kGT * 24 + t * 16;
+    cp16(bx, p, v ? 16u : 0u);
+    cp16(bx + kGT * 16, p + 4, v ? 16u : 0u);
+}
+
+// The raw share of matrix j in a raw stage, as an ARaw.
+template <int NM>
+__device__ __forceinline__ ARaw raw_a(const ASrc &s, const uint8_t *raw, int j) {
+    ARaw R;
+    R.type = s.type;
+    R.d = R.mn = 0.f;
+    R.w = make_uint4(0u, 0u, 0u, 0u);
+    if (!s.type) return R;
+    const int t = threadIdx.x;
+    R.w = *reinterpret_cast<const uint4 *>(raw + (j * kGT + t) * 16);
+    const uint2 dw = *reinterpret_cast<const uint2 *>(raw + NM * kGT * 16 + (j * kGT + t) * 8);
+    R.d = __half2float(__ushort_as_half((unsigned short)(s.hi ? dw.x >> 16 : dw.x & 0xFFFFu)));
+    if (s.type == 3) R.mn = __half2float(__ushort_as_half((unsigned short)(s.hi ? dw.y >> 16 : dw.y & 0xFFFFu)));
+    return R;
 }
 
 // The raw share dequantised exactly in float32 and split into the NP bf16
@@ -616,21 +692,6 @@ __device__ __forceinline__ void stage_a(const ARaw &R, uint8_t *a) {
     const bool q8 = R.type == 8;
     store_split8<NP>(a, cm_off(row, q8 ? 2 * h : h, kMR / 8), kAPiece, lo);
     store_split8<NP>(a, cm_off(row, q8 ? 2 * h + 1 : 2 + h, kMR / 8), kAPiece, hi);
-}
-
-// A thread's share of one activation block: token t / 4, columns 8 (t % 4)..+7
-// (and, with a norm, the 8 norm weights of those columns).
-__device__ __forceinline__ void load_b(const float *x, const float *nw, int K, int m, int kb, float4 (&u)[4]) {
-    const int tok = threadIdx.x >> 2, c = threadIdx.x & 3;
-    u[0] = u[1] = u[2] = u[3] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (tok < m) {
-        const float4 *p = reinterpret_cast<const float4 *>(x + (size_t)tok * K + kb * 32 + 8 * c);
-        u[0] = __ldcg(p), u[1] = __ldcg(p + 1);
-        if (nw) {
-            const float4 *q = reinterpret_cast<const float4 *>(nw + kb * 32 + 8 * c);
-            u[2] = __ldg(q), u[3] = __ldg(q + 1);
-        }
-    }
 }
 
 // The block into the three B pieces; with a norm, each value is (x * s) * w
@@ -709,18 +770,24 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
         int tot[2] = {0, 0};
         for (int i = 0; i < ga.a.nm; ++i) tot[0] += ga.a.m[i].rows;
         for (int i = 0; i < (NM == 2 ? ga.b.nm : 0); ++i) tot[1] += ga.b.m[i].rows;
-        // Block i's raw operands are loaded during block i - 1 into the other of two register sets (two
-        // blocks per pass, so that no set is copied: a copy would wait for the loads).
-        ARaw ra[2][NM];
-        float4 xb[2][4];
+        // Raw operands travel by cp.async kDepth - 1 blocks ahead of their staging; each thread copies the
+        // raw bytes it dequantises itself, so its own cp.async group waits are all the ordering needed.
+        ASrc as[NM];
+        for (int j = 0; j < NM; ++j) a_src(j == 0 ? ga.a : ga.b, tot[j], r0, as[j]);
         const bool norm = ga.norm_w != nullptr;
-        if (nblk > 0) {
-            for (int j = 0; j < NM; ++j) load_a(j == 0 ? ga.a : ga.b, tot[j], r0, kb0, ra[0][j]);
-            load_b(ga.x, ga.norm_w, K, ga.m, kb0, xb[0]);
+        const float *s_nw = reinterpret_cast<const float *>(tsm + nw_off(NM));
+        const uint32_t raw0 = su32(tsm + raw_off(NM));
+        if (norm)  // the norm weights of the CTA's K range (the oldest group)
+            for (int i = threadIdx.x; i < nblk * 8; i += kGT) cp16(su32(s_nw) + i * 16, ga.norm_w + kb0 * 32 + i * 4);
+        cp_commit();
+#pragma unroll
+        for (int p = 0; p < kDepth - 1; ++p) {
+            if (p < nblk) copy_raw<NM>(as, ga.x, K, ga.m, kb0 + p, raw0 + p * raw_bytes(NM));
+            cp_commit();
         }
         // RMSNorm scale of each token (cpu.go:81-98: 1 / sqrt(mean of squares + eps) in double, rounded
         // to float), from the row's sums of squares per 128-row tile, added in tile order; read while the
-        // first block's operands load, then shared by the staging warps (named barrier 1)
+        // first blocks' operands load, then shared by the staging warps with the norm weights (named barrier 1)
         float sn = 1.f;
         if (norm) {
             if ((int)threadIdx.x < ga.m) {
@@ -729,37 +796,46 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
                 for (int i = 0; i < ntiles; ++i) ss += __ldcg(dm.ssq + (size_t)threadIdx.x * kSsqTiles + i);
                 s_norm[threadIdx.x] = (float)(1.0 / sqrt((double)__fadd_rn(__fdiv_rn(ss, (float)(ga.nb * 32)), dm.eps)));
             }
+            cp_wait<kDepth - 1>();  // this thread's norm-weight copies have landed
             asm volatile("bar.sync 1, %0;" ::"n"(kGT) : "memory");
             if ((int)(threadIdx.x >> 2) < ga.m) sn = s_norm[threadIdx.x >> 2];
         }
-        auto step = [&](int i, int cur) {
+        const int c8 = 8 * (threadIdx.x & 3);
+        for (int i = 0; i < nblk; ++i) {
+            const int pf = i + kDepth - 1;
+            if (pf < nblk) copy_raw<NM>(as, ga.x, K, ga.m, kb0 + pf, raw0 + (pf % kDepth) * raw_bytes(NM));
+            cp_commit();
+            cp_wait<kDepth - 1>();  // block i's raw operands (this thread's copies) have landed
             const int st = i & 1;
             uint8_t *stage = tsm + st * stage_bytes(NM);
-            if (i + 1 < nblk) {
-                for (int j = 0; j < NM; ++j) load_a(j == 0 ? ga.a : ga.b, tot[j], r0, kb0 + i + 1, ra[cur ^ 1][j]);
-                load_b(ga.x, ga.norm_w, K, ga.m, kb0 + i + 1, xb[cur ^ 1]);
-            }
             if (i >= 2) {  // the MMAs of block i - 2 have read this stage (one wait per warp)
                 bool w = true;
                 if (lane == 0) w = bar_wait(empty + st, ((i >> 1) - 1) & 1, dm.err);
                 if (!__shfl_sync(kFull, w, 0)) {
                     ok = false;
-                    return;
+                    break;
                 }
             }
+            const uint8_t *raw = tsm + raw_off(NM) + (i % kDepth) * raw_bytes(NM);
             for (int j = 0; j < NM; ++j) {
-                if (np == 3) stage_a<3>(ra[cur][j], stage + j * 3 * kAPiece);
-                else stage_a<2>(ra[cur][j], stage + j * 3 * kAPiece);
+                const ARaw R = raw_a<NM>(as[j], raw, j);
+                if (np == 3) stage_a<3>(R, stage + j * 3 * kAPiece);
+                else stage_a<2>(R, stage + j * 3 * kAPiece);
             }
-            stage_b(xb[cur], norm, sn, stage + NM * 3 * kAPiece);
+            float4 xb[4];
+            const uint8_t *bx = raw + NM * kGT * 24 + threadIdx.x * 16;
+            xb[0] = *reinterpret_cast<const float4 *>(bx);
+            xb[1] = *reinterpret_cast<const float4 *>(bx + kGT * 16);
+            if (norm) {
+                const float4 *w4 = reinterpret_cast<const float4 *>(s_nw + (size_t)i * 32 + c8);
+                xb[2] = w4[0], xb[3] = w4[1];
+            }
+            stage_b(xb, norm, sn, stage + NM * 3 * kAPiece);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the operands, to the tensor cores' proxy
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(full + st)) : "memory");
-        };
-        for (int i = 0; i < nblk && ok; i += 2) {
-            step(i, 0);
-            if (ok && i + 1 < nblk) step(i + 1, 1);
         }
+        cp_wait<0>();  // nothing left in flight (the error path leaves copies behind)
     } else if (lane == 0) {
         // descriptors of stage 0, piece 0, K step 0 (the others are byte offsets added to the address field)
         const uint64_t da0 = sdesc(su32(tsm), (kMR / 8) * 128, 128);
@@ -949,12 +1025,29 @@ cudaError_t gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, k_gemm<EPI>, ga);
 }
 
+// Clusters of s CTAs (s = 1, 2, 4, 8) of each tensor-core product kernel that
+// are resident at once, by device (cudaOccupancyMaxActiveClusters: one CTA
+// per SM, and a cluster's CTAs in one GPC), measured by prepare_products.
+constexpr int kMaxDevices = 64;
+int g_mma_clusters[kMaxDevices][4][4];
+
+// CTAs along K per row tile for the tensor-core products: the largest of 8,
+// 4, 2 whose clusters are all resident at once (a second wave would double
+// the time) and that gives each CTA at least 2 K blocks.
+int mma_splits(int epi, int row_tiles, int nb) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+    for (int s = 8, ix = 3; s > 1; s /= 2, --ix)
+        if (nb >= 2 * s && row_tiles <= g_mma_clusters[dev][epi][ix]) return s;
+    return 1;
+}
+
 template <int EPI>
 cudaError_t mma_gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
     GemmArgs ga = base;
     const int row_tiles = (rows + tc::kMR - 1) / tc::kMR;
-    ga.splits = EPI == EPI_ARGMAX ? 1 : splits_for(row_tiles, ga.nb, nsm);
+    ga.splits = EPI == EPI_ARGMAX ? 1 : mma_splits(EPI, row_tiles, ga.nb);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(row_tiles, ga.splits);
     cfg.blockDim = dim3(kMT);
@@ -984,6 +1077,29 @@ cudaError_t prepare_products() {
         const cudaError_t e = cudaFuncSetAttribute(f.first, cudaFuncAttributeMaxDynamicSharedMemorySize, f.second);
         if (e != cudaSuccess) return e;
     }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    for (int k = 0; k < 4; ++k)
+        for (int ix = 0; ix < 4; ++ix) {
+            const int s = 1 << ix;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(1, s);
+            cfg.blockDim = dim3(kMT);
+            cfg.dynamicSmemBytes = fs[k].second;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = s, attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, fs[k].first, &cfg);
+            if (e != cudaSuccess) return e;
+            g_mma_clusters[dev][k][ix] = n;
+        }
     return cudaSuccess;
 }
 
