@@ -560,7 +560,16 @@ __device__ __forceinline__ void store_split8(uint8_t *base, uint32_t off, int ps
     for (int j = 0; j < NP; ++j) *reinterpret_cast<uint4 *>(base + j * pstride + off) = make_uint4(p[j][0], p[j][1], p[j][2], p[j][3]);
 }
 
-// A thread's raw share of one weight block: row t / 2, half t % 2 of its
+// Staging thread t takes weight row t % 128, half t / 128 of each block, and
+// token t % 64, columns 8 (t / 64)..+7 of the activations: consecutive
+// threads then store consecutive 16-byte rows of a core matrix, which is free
+// of shared-memory bank conflicts.
+__device__ __forceinline__ int a_row() { return threadIdx.x & (kMR - 1); }
+__device__ __forceinline__ int a_half() { return threadIdx.x >> 7; }
+__device__ __forceinline__ int b_tok() { return threadIdx.x & (kMN - 1); }
+__device__ __forceinline__ int b_col8() { return threadIdx.x >> 6; }
+
+// A thread's raw share of one weight block: row a_row(), half a_half() of its
 // quants (Q4: bytes 8h..8h+7; Q8_0: bytes 16h..16h+15), its scale and (Q4_1)
 // minimum.
 struct ARaw {
@@ -579,7 +588,7 @@ struct ASrc {
 };
 
 __device__ __forceinline__ void a_src(const MatSet &ms, int total, int r0, ASrc &s) {
-    const int row = threadIdx.x >> 1, h = threadIdx.x & 1;
+    const int row = a_row(), h = a_half();
     s.q = s.d = nullptr;
     s.type = s.hi = s.qstep = s.mstep = 0;
     if (r0 + row >= total) return;
@@ -613,8 +622,8 @@ __device__ __forceinline__ void cp_wait() {
 }
 
 // This thread's raw operands of block kb into the raw stage at shared address
-// raw: its weight shares (as[j]) and its 8 activations (token t / 4, columns
-// 8 (t % 4)..+7; zeros for tokens past m).
+// raw: its weight shares (as[j]) and its 8 activations (token b_tok(), columns
+// 8 b_col8()..+7; zeros for tokens past m).
 template <int NM>
 __device__ __forceinline__ void copy_raw(const ASrc (&as)[NM], const float *x, int K, int m, int kb, uint32_t raw) {
     const int t = threadIdx.x;
@@ -629,7 +638,7 @@ __device__ __forceinline__ void copy_raw(const ASrc (&as)[NM], const float *x, i
         cp4(ad, d);
         if (s.type == 3) cp4(ad + 4, d + s.mstep);
     }
-    const int tok = t >> 2, c = t & 3;
+    const int tok = b_tok(), c = b_col8();
     const bool v = tok < m;
     const float *p = v ? x + (size_t)tok * K + kb * 32 + 8 * c : x;
     const uint32_t bx = raw + NM * kGT * 24 + t * 16;
@@ -659,7 +668,7 @@ __device__ __forceinline__ ARaw raw_a(const ASrc &s, const uint8_t *raw, int j) 
 // row is zero.
 template <int NP>
 __device__ __forceinline__ void stage_a(const ARaw &R, uint8_t *a) {
-    const int row = threadIdx.x >> 1, h = threadIdx.x & 1;
+    const int row = a_row(), h = a_half();
     float lo[8], hi[8];
     if (R.type == 0) {
 #pragma unroll
@@ -697,7 +706,7 @@ __device__ __forceinline__ void stage_a(const ARaw &R, uint8_t *a) {
 // The block into the three B pieces; with a norm, each value is (x * s) * w
 // first (cpu.go:94-97's rounding points), s the token's 1 / rms.
 __device__ __forceinline__ void stage_b(const float4 (&u)[4], bool norm, float s, uint8_t *b) {
-    const int tok = threadIdx.x >> 2, c = threadIdx.x & 3;
+    const int tok = b_tok(), c = b_col8();
     float v[8] = {u[0].x, u[0].y, u[0].z, u[0].w, u[1].x, u[1].y, u[1].z, u[1].w};
     if (norm) {
         const float w[8] = {u[2].x, u[2].y, u[2].z, u[2].w, u[3].x, u[3].y, u[3].z, u[3].w};
@@ -798,9 +807,9 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
             }
             cp_wait<kDepth - 1>();  // this thread's norm-weight copies have landed
             asm volatile("bar.sync 1, %0;" ::"n"(kGT) : "memory");
-            if ((int)(threadIdx.x >> 2) < ga.m) sn = s_norm[threadIdx.x >> 2];
+            if (b_tok() < ga.m) sn = s_norm[b_tok()];
         }
-        const int c8 = 8 * (threadIdx.x & 3);
+        const int c8 = 8 * b_col8();
         for (int i = 0; i < nblk; ++i) {
             const int pf = i + kDepth - 1;
             if (pf < nblk) copy_raw<NM>(as, ga.x, K, ga.m, kb0 + pf, raw0 + (pf % kDepth) * raw_bytes(NM));
