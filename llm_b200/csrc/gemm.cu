@@ -729,6 +729,107 @@ __device__ __forceinline__ void stage_b(const float4 (&u)[4], bool norm, float s
 
 }  // namespace tc
 
+// The tensor-core products' epilogue, split in two: epi_in gathers an item's
+// inputs that do not depend on the product (destination, QKV bias and RoPE
+// (cos, sin), the residual's old values), so that a CTA can load them while
+// its MMAs finish and its cluster meets; epi_out applies them to the item's
+// 4 summed rows, as epilogue() does.
+struct EpiIn {
+    float *dst;    // the item's first output element
+    float a[4];    // QKV: the bias; RESID: the residual rows' old values
+    float2 cs[2];  // QKV: (cos, sin) of the item's two rotary pairs
+    int n;         // outputs of the item (0: none)
+    bool hasb, rot;
+};
+
+template <int EPI>
+__device__ __forceinline__ EpiIn epi_in(const GemmArgs &ga, const DevModel &dm, int g, int t, int total) {
+    EpiIn e;
+    e.dst = nullptr;
+    e.n = 0;
+    e.hasb = e.rot = false;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) e.a[c] = 0.f;
+    e.cs[0] = e.cs[1] = make_float2(0.f, 0.f);
+    if (t >= ga.m || g >= total) return e;
+    int la = 0;
+    const int seg = mat_of(ga.a, g, la);
+    const QMat &ma = ga.a.m[seg];
+    if constexpr (EPI == EPI_RESID) {
+        e.n = min(4, ma.rows - la);
+        e.dst = ga.out + (size_t)t * ga.out_ld + g;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (c < e.n) e.a[c] = __ldcg(e.dst + c);
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        e.n = max(0, min(4, min(dm.ff, ma.rows) - g));
+        e.dst = ga.out + (size_t)t * ga.out_ld + g;
+    } else if constexpr (EPI == EPI_QKV) {  // kernels_fused.go:212-224; cpu.go:279-303
+        const int pos = ga.tb ? ga.tb->pos[t] : (int)dm.state[0] + t;
+        const Layer &L = dm.layer[ga.l];
+        const float *bias = seg == 0 ? L.bq : seg == 1 ? L.bk : L.bv;
+        e.hasb = bias != nullptr;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (bias) e.a[c] = __ldg(bias + la + c);
+        e.rot = seg < 2;
+        if (seg < 2) {
+            const int hp = dm.head_dim >> 1;
+#pragma unroll
+            for (int c = 0; c < 4; c += 2)
+                e.cs[c >> 1] = __ldg(reinterpret_cast<const float2 *>(dm.rope_cs) + (size_t)pos * hp +
+                                     (((la + c) % dm.head_dim) >> 1));
+        }
+        float *kv = ga.tb ? ga.tb->kv + ((size_t)ga.tb->slot[t] * ga.tb->layers + ga.l) * 2 * (size_t)dm.ctx * dm.kvd
+                          : L.kv;
+        e.dst = seg == 0 ? dm.q + (size_t)t * dm.embd + la
+                         : kv + ((seg == 1 ? 0 : (size_t)dm.ctx) + pos) * (size_t)dm.kvd + la;
+        e.n = 4;
+    }
+    return e;
+}
+
+// Applies an item's inputs to its summed rows v; returns the sum of squares of a residual's new values.
+template <int EPI, int NM>
+__device__ __forceinline__ float epi_out(const EpiIn &e, const float (&v)[NM][4]) {
+    float sq = 0.f;
+    if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (c < e.n) {
+                const float nv = __fadd_rn(e.a[c], v[0][c]);
+                e.dst[c] = nv;
+                sq = fmaf(nv, nv, sq);
+            }
+    } else if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (c < e.n) {
+                const float g = v[0][c], u = v[NM - 1][c];
+                const float den = __fadd_rn(1.f, (float)exp(-(double)g));  // cpu.go:345
+                e.dst[c] = __fmul_rn(__fdiv_rn(g, den), u);
+            }
+    } else if constexpr (EPI == EPI_QKV) {
+        if (e.n) {
+            float o[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[c] = e.hasb ? __fadd_rn(v[0][c], e.a[c]) : v[0][c];
+            if (e.rot) {  // rotate adjacent pairs (cpu.go:371-385)
+#pragma unroll
+                for (int c = 0; c < 4; c += 2) {
+                    const float2 cs = e.cs[c >> 1];
+                    const float x0 = o[c], x1 = o[c + 1];
+                    o[c] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+                    o[c + 1] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) e.dst[c] = o[c];
+        }
+    }
+    return sq;
+}
+
 // grid (row tiles of 128, splits), cluster (1, splits, 1); 9 warps.  NM
 // matrices (2: gate and up) share the activations; each has its own
 // accumulator (64 tensor-memory columns).  Warps 0-7 stage the operands of
@@ -775,6 +876,19 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_slot;
     bool ok = true;
+    // epilogue work items, token-major (t = it / 32, u = it % 32), CTA sp taking a contiguous share, so that
+    // a warp's threads cover consecutive 4-row groups of one token (coalesced epilogue stores).  With
+    // ssq_out (a residual product) CTA sp takes whole tokens, a warp per token, so that the warp can sum
+    // the squares of its token's new rows.
+    const int S = ga.splits;
+    const bool tok_rows = EPI == EPI_RESID && ga.ssq_out;
+    const int items = (kMR / 4) * ga.m;
+    const int i0 = tok_rows ? 32 * (ga.m * sp / S) : items * sp / S;
+    const int i1 = tok_rows ? 32 * (ga.m * (sp + 1) / S) : items * (sp + 1) / S;
+    int total = 0;
+    for (int i = 0; i < ga.a.nm; ++i) total += ga.a.m[i].rows;
+    EpiIn pre;  // the inputs of this thread's first item, loaded once its operands are staged
+    pre.n = 0;
     if (!mma_warp) {
         int tot[2] = {0, 0};
         for (int i = 0; i < ga.a.nm; ++i) tot[0] += ga.a.m[i].rows;
@@ -845,6 +959,10 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(full + st)) : "memory");
         }
         cp_wait<0>();  // nothing left in flight (the error path leaves copies behind)
+        if constexpr (EPI != EPI_ARGMAX) {
+            const int it = i0 + (int)threadIdx.x;
+            if (it < i1) pre = epi_in<EPI>(ga, dm, r0 + 4 * (it & 31), it >> 5, total);
+        }
     } else if (lane == 0) {
         // descriptors of stage 0, piece 0, K step 0 (the others are byte offsets added to the address field)
         const uint64_t da0 = sdesc(su32(tsm), (kMR / 8) * 128, 128);
@@ -929,75 +1047,40 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
         // the cluster's partials summed in rank order, then the epilogue: work item (4-row group u, token t)
         cg::cluster_group cl = cg::this_cluster();
         if (ga.splits > 1) cl.sync();
-        const int S = ga.splits;
-        // items token-major (t = it / 32, u = it % 32), CTA sp taking a contiguous share, so that a warp's
-        // threads cover consecutive 4-row groups of one token (coalesced epilogue stores).  With ssq_out
-        // (a residual product) CTA sp takes whole tokens, a warp per token, so that the warp can sum the
-        // squares of its token's new rows.
-        const int items = (kMR / 4) * ga.m;
-        const bool tok_rows = EPI == EPI_RESID && ga.ssq_out;
-        const int i0 = tok_rows ? 32 * (ga.m * sp / S) : items * sp / S;
-        const int i1 = tok_rows ? 32 * (ga.m * (sp + 1) / S) : items * (sp + 1) / S;
-        int total = 0;
-        for (int i = 0; i < ga.a.nm; ++i) total += ga.a.m[i].rows;
         // (with tok_rows i0 is a multiple of 32, so every warp's 32 items are one token's)
         for (int it = i0 + (int)threadIdx.x; ok && !mma_warp && it < i1; it += kGT) {
             const int t = it >> 5, u = it & 31;
             const int g = r0 + 4 * u;
-            if (tok_rows) {
-                // a warp per token: every lane takes part in the sum (rows past the matrix add 0)
-                float sq = 0.f;
-                if (g < total) {
-                    float4 pv[8];
+            const EpiIn e = it == i0 + (int)threadIdx.x ? pre : epi_in<EPI>(ga, dm, g, t, total);
+            float sq = 0.f;
+            if (g < total) {
+                // every rank's float4 of rows 4u..4u+3 at token t loaded first, then summed in rank order
+                float4 pv[8][NM];
 #pragma unroll
-                    for (int r = 0; r < 8; ++r)
-                        if (r < S) {
-                            const float *rs = S > 1 ? cl.map_shared_rank(part, r) : part;
-                            pv[r] = *reinterpret_cast<const float4 *>(rs + (size_t)t * kPartLd + 4 * u);
-                        }
-                    float v[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int r = 0; r < 8; ++r) {
+                    if (r < S) {
+                        const float *rs = S > 1 ? cl.map_shared_rank(part, r) : part;
 #pragma unroll
-                    for (int r = 0; r < 8; ++r)
-                        if (r < S) v[0] += pv[r].x, v[1] += pv[r].y, v[2] += pv[r].z, v[3] += pv[r].w;
-                    int la = 0;
-                    const QMat &ma = ga.a.m[mat_of(ga.a, g, la)];
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        if (la + c >= ma.rows) continue;
-                        float *p = ga.out + (size_t)t * ga.out_ld + g + c;
-                        const float nv = __fadd_rn(__ldcg(p), v[c]);
-                        *p = nv;
-                        sq = fmaf(nv, nv, sq);
+                        for (int j = 0; j < NM; ++j)
+                            pv[r][j] = *reinterpret_cast<const float4 *>(rs + ((size_t)j * kMN + t) * kPartLd + 4 * u);
                     }
                 }
+                float v[NM][4];
+#pragma unroll
+                for (int j = 0; j < NM; ++j) {
+                    v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
+#pragma unroll
+                    for (int r = 0; r < 8; ++r)
+                        if (r < S) v[j][0] += pv[r][j].x, v[j][1] += pv[r][j].y, v[j][2] += pv[r][j].z, v[j][3] += pv[r][j].w;
+                }
+                sq = epi_out<EPI, NM>(e, v);
+            }
+            if (tok_rows) {
+                // a warp per token: every lane takes part in the sum (rows past the matrix add 0)
 #pragma unroll
                 for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
                 if (u == 0) dm.ssq[(size_t)t * kSsqTiles + rt] = sq;
-                continue;
             }
-            if (g >= total) continue;
-            // every rank's float4 of rows 4u..4u+3 at token t loaded first, then summed in rank order
-            float4 pv[8][NM];
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                if (r < S) {
-                    const float *rs = S > 1 ? cl.map_shared_rank(part, r) : part;
-#pragma unroll
-                    for (int j = 0; j < NM; ++j)
-                        pv[r][j] = *reinterpret_cast<const float4 *>(rs + ((size_t)j * kMN + t) * kPartLd + 4 * u);
-                }
-            }
-            float v[NM][4];
-#pragma unroll
-            for (int j = 0; j < NM; ++j) {
-                v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
-#pragma unroll
-                for (int r = 0; r < 8; ++r)
-                    if (r < S) v[j][0] += pv[r][j].x, v[j][1] += pv[r][j].y, v[j][2] += pv[r][j].z, v[j][3] += pv[r][j].w;
-            }
-            int la = 0;
-            const int seg = mat_of(ga.a, g, la);
-            epilogue<EPI, NM>(ga, dm, ga.a.m[seg], seg, la, g, t, 0, v);
         }
         if (ga.splits > 1) cl.sync();  // the partials stay readable until every CTA of the cluster is done
     }
