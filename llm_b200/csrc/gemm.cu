@@ -56,17 +56,25 @@ struct MatSet {
     int nm;
 };
 
+// (Unrolled over the 3 slots, so that the descriptors are read at fixed
+// offsets of the kernel parameter, not through a computed address.)
 __device__ __forceinline__ int mat_of(const MatSet &ms, int g, int &local) {
     int base = 0;
-    for (int j = 0; j < ms.nm; ++j) {
-        if (g < base + ms.m[j].rows) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        if (j < ms.nm && g < base + ms.m[j].rows) {
             local = g - base;
             return j;
         }
-        base += ms.m[j].rows;
+        if (j < ms.nm) base += ms.m[j].rows;
     }
     local = 0;
     return ms.nm - 1;
+}
+
+// Descriptor j of a set, read at a fixed offset (see mat_of).
+__device__ __forceinline__ const QMat &mat_at(const MatSet &ms, int j) {
+    return j == 0 ? ms.m[0] : j == 1 ? ms.m[1] : ms.m[2];
 }
 
 // One thread's share of a weight block: row t / 4 of the tile, quarter t % 4
@@ -233,7 +241,7 @@ __global__ void __launch_bounds__(kGT) k_gemm(const __grid_constant__ GemmArgs g
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     int la = 0, lb = 0;
     const int seg = mat_of(ga.a, r0, la);
-    const QMat &ma = ga.a.m[seg];
+    const QMat &ma = mat_at(ga.a, seg);
     const QMat &mb = ga.b.m[NM == 2 ? mat_of(ga.b, r0, lb) : 0];
     const int kb0 = ga.nb * sp / ga.splits, kb1 = ga.nb * (sp + 1) / ga.splits;  // balanced K share
     const int K = ga.nb * 32;
@@ -593,7 +601,7 @@ __device__ __forceinline__ void a_src(const MatSet &ms, int total, int r0, ASrc 
     s.type = s.hi = s.qstep = s.mstep = 0;
     if (r0 + row >= total) return;
     int lr = 0;
-    const QMat &m = ms.m[mat_of(ms, r0 + row, lr)];
+    const QMat &m = mat_at(ms, mat_of(ms, r0 + row, lr));
     const uint8_t *tile = m.tiles + (size_t)(lr >> 3) * m.tile_bytes;
     const int r = lr & 7;
     const bool q8 = m.type == 8;
@@ -754,7 +762,7 @@ __device__ __forceinline__ EpiIn epi_in(const GemmArgs &ga, const DevModel &dm, 
     if (t >= ga.m || g >= total) return e;
     int la = 0;
     const int seg = mat_of(ga.a, g, la);
-    const QMat &ma = ga.a.m[seg];
+    const QMat &ma = mat_at(ga.a, seg);
     if constexpr (EPI == EPI_RESID) {
         e.n = min(4, ma.rows - la);
         e.dst = ga.out + (size_t)t * ga.out_ld + g;
@@ -895,9 +903,17 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
         for (int i = 0; i < (NM == 2 ? ga.b.nm : 0); ++i) tot[1] += ga.b.m[i].rows;
         // Raw operands travel by cp.async kDepth - 1 blocks ahead of their staging; each thread copies the
         // raw bytes it dequantises itself, so its own cp.async group waits are all the ordering needed.
+        // RMSNorm inputs first: each token's sums of squares per 128-row tile (their loads overlap the
+        // set-up below)
+        const bool norm = ga.norm_w != nullptr;
+        const int ntiles = (ga.nb * 32 + kMR - 1) / kMR;
+        float ssv[kSsqTiles];
+#pragma unroll
+        for (int i = 0; i < kSsqTiles; ++i)
+            ssv[i] = norm && (int)threadIdx.x < ga.m && i < ntiles ? __ldcg(dm.ssq + (size_t)threadIdx.x * kSsqTiles + i)
+                                                                    : 0.f;
         ASrc as[NM];
         for (int j = 0; j < NM; ++j) a_src(j == 0 ? ga.a : ga.b, tot[j], r0, as[j]);
-        const bool norm = ga.norm_w != nullptr;
         const float *s_nw = reinterpret_cast<const float *>(tsm + nw_off(NM));
         const uint32_t raw0 = su32(tsm + raw_off(NM));
         if (norm)  // the norm weights of the CTA's K range (the oldest group)
@@ -909,14 +925,15 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
             cp_commit();
         }
         // RMSNorm scale of each token (cpu.go:81-98: 1 / sqrt(mean of squares + eps) in double, rounded
-        // to float), from the row's sums of squares per 128-row tile, added in tile order; read while the
-        // first blocks' operands load, then shared by the staging warps with the norm weights (named barrier 1)
+        // to float), from the row's sums of squares per 128-row tile, added in tile order, then shared by
+        // the staging warps with the norm weights (named barrier 1)
         float sn = 1.f;
         if (norm) {
             if ((int)threadIdx.x < ga.m) {
-                const int ntiles = (ga.nb * 32 + kMR - 1) / kMR;
                 float ss = 0.f;
-                for (int i = 0; i < ntiles; ++i) ss += __ldcg(dm.ssq + (size_t)threadIdx.x * kSsqTiles + i);
+#pragma unroll
+                for (int i = 0; i < kSsqTiles; ++i)
+                    if (i < ntiles) ss += ssv[i];
                 s_norm[threadIdx.x] = (float)(1.0 / sqrt((double)__fadd_rn(__fdiv_rn(ss, (float)(ga.nb * 32)), dm.eps)));
             }
             cp_wait<kDepth - 1>();  // this thread's norm-weight copies have landed
