@@ -629,11 +629,11 @@ __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// This thread's raw operands of block kb into the raw stage at shared address
-// raw: its weight shares (as[j]) and its 8 activations (token b_tok(), columns
-// 8 b_col8()..+7; zeros for tokens past m).
+// This thread's raw weight shares (as[j]) of block kb into the raw stage at
+// shared address raw.  The weights are constant, so these copies may precede
+// the wait for the previous kernel.
 template <int NM>
-__device__ __forceinline__ void copy_raw(const ASrc (&as)[NM], const float *x, int K, int m, int kb, uint32_t raw) {
+__device__ __forceinline__ void copy_raw_a(const ASrc (&as)[NM], int kb, uint32_t raw) {
     const int t = threadIdx.x;
 #pragma unroll
     for (int j = 0; j < NM; ++j) {
@@ -646,13 +646,25 @@ __device__ __forceinline__ void copy_raw(const ASrc (&as)[NM], const float *x, i
         cp4(ad, d);
         if (s.type == 3) cp4(ad + 4, d + s.mstep);
     }
+}
+
+// This thread's 8 activations of block kb (token b_tok(), columns 8 b_col8()..+7;
+// zeros for tokens past m) into the raw stage at shared address raw.
+template <int NM>
+__device__ __forceinline__ void copy_raw_b(const float *x, int K, int m, int kb, uint32_t raw) {
     const int tok = b_tok(), c = b_col8();
     const bool v = tok < m;
     const float *p = v ? x + (size_t)tok * K + kb * 32 + 8 * c : x;
-    const uint32_t bx = raw + NM * kGT * 24 + t * 16;
+    const uint32_t bx = raw + NM * kGT * 24 + threadIdx.x * 16;
     cp16(bx, p, v ? 16u : 0u);
     cp16(bx + kGT * 16, p + 4, v ? 16u : 0u);
 }
+
+// Programmatic dependent launch: wait until the grids this one depends on
+// have completed and their writes are visible (a no-op without such a
+// dependency), and allow the dependent grid to launch.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // The raw share of matrix j in a raw stage, as an ARaw.
 template <int NM>
@@ -903,25 +915,31 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
         for (int i = 0; i < (NM == 2 ? ga.b.nm : 0); ++i) tot[1] += ga.b.m[i].rows;
         // Raw operands travel by cp.async kDepth - 1 blocks ahead of their staging; each thread copies the
         // raw bytes it dequantises itself, so its own cp.async group waits are all the ordering needed.
-        // RMSNorm inputs first: each token's sums of squares per 128-row tile (their loads overlap the
-        // set-up below)
+        // The constant operands of the first blocks (weights, norm weights) are requested before the wait
+        // for the previous kernel, whose outputs (activations, sums of squares) are read after it.
+        // Groups: {weights of blocks 0..kDepth-2, norm weights, activations of block 0}, then the
+        // activations of blocks 1..kDepth-2, then {weights, activations} of each later block.
         const bool norm = ga.norm_w != nullptr;
         const int ntiles = (ga.nb * 32 + kMR - 1) / kMR;
+        ASrc as[NM];
+        for (int j = 0; j < NM; ++j) a_src(j == 0 ? ga.a : ga.b, tot[j], r0, as[j]);
+        const float *s_nw = reinterpret_cast<const float *>(tsm + nw_off(NM));
+        const uint32_t raw0 = su32(tsm + raw_off(NM));
+#pragma unroll
+        for (int p = 0; p < kDepth - 1; ++p)
+            if (p < nblk) copy_raw_a<NM>(as, kb0 + p, raw0 + p * raw_bytes(NM));
+        if (norm)  // the norm weights of the CTA's K range
+            for (int i = threadIdx.x; i < nblk * 8; i += kGT) cp16(su32(s_nw) + i * 16, ga.norm_w + kb0 * 32 + i * 4);
+        griddep_wait();
+        // RMSNorm inputs: each token's sums of squares per 128-row tile
         float ssv[kSsqTiles];
 #pragma unroll
         for (int i = 0; i < kSsqTiles; ++i)
             ssv[i] = norm && (int)threadIdx.x < ga.m && i < ntiles ? __ldcg(dm.ssq + (size_t)threadIdx.x * kSsqTiles + i)
                                                                     : 0.f;
-        ASrc as[NM];
-        for (int j = 0; j < NM; ++j) a_src(j == 0 ? ga.a : ga.b, tot[j], r0, as[j]);
-        const float *s_nw = reinterpret_cast<const float *>(tsm + nw_off(NM));
-        const uint32_t raw0 = su32(tsm + raw_off(NM));
-        if (norm)  // the norm weights of the CTA's K range (the oldest group)
-            for (int i = threadIdx.x; i < nblk * 8; i += kGT) cp16(su32(s_nw) + i * 16, ga.norm_w + kb0 * 32 + i * 4);
-        cp_commit();
 #pragma unroll
         for (int p = 0; p < kDepth - 1; ++p) {
-            if (p < nblk) copy_raw<NM>(as, ga.x, K, ga.m, kb0 + p, raw0 + p * raw_bytes(NM));
+            if (p < nblk) copy_raw_b<NM>(ga.x, K, ga.m, kb0 + p, raw0 + p * raw_bytes(NM));
             cp_commit();
         }
         // RMSNorm scale of each token (cpu.go:81-98: 1 / sqrt(mean of squares + eps) in double, rounded
@@ -936,14 +954,17 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
                     if (i < ntiles) ss += ssv[i];
                 s_norm[threadIdx.x] = (float)(1.0 / sqrt((double)__fadd_rn(__fdiv_rn(ss, (float)(ga.nb * 32)), dm.eps)));
             }
-            cp_wait<kDepth - 1>();  // this thread's norm-weight copies have landed
+            cp_wait<kDepth - 2>();  // this thread's norm-weight copies (the oldest group) have landed
             asm volatile("bar.sync 1, %0;" ::"n"(kGT) : "memory");
             if (b_tok() < ga.m) sn = s_norm[b_tok()];
         }
         const int c8 = 8 * b_col8();
         for (int i = 0; i < nblk; ++i) {
             const int pf = i + kDepth - 1;
-            if (pf < nblk) copy_raw<NM>(as, ga.x, K, ga.m, kb0 + pf, raw0 + (pf % kDepth) * raw_bytes(NM));
+            if (pf < nblk) {
+                copy_raw_a<NM>(as, kb0 + pf, raw0 + (pf % kDepth) * raw_bytes(NM));
+                copy_raw_b<NM>(ga.x, K, ga.m, kb0 + pf, raw0 + (pf % kDepth) * raw_bytes(NM));
+            }
             cp_commit();
             cp_wait<kDepth - 1>();  // block i's raw operands (this thread's copies) have landed
             const int st = i & 1;
@@ -1015,6 +1036,7 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
         ok = __shfl_sync(kFull, w, 0);
     }
     ok = !__syncthreads_or(!ok);
+    griddep_launch();  // the next kernel may start its own set-up while this one reduces and stores
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     // accumulators -> part[j][token][row] (token-major, so that 4 consecutive rows of a token are one float4;
     // the stages are free): warp w < 8 reads lanes 32 (w % 4).. of columns 32 (w / 4)..
@@ -1151,8 +1173,13 @@ int mma_splits(int epi, int row_tiles, int nb) {
     return 1;
 }
 
+// pdl: launched as a programmatic dependent of the previous kernel in the
+// stream, which lets it in once all of that kernel's CTAs have finished their
+// MMAs (k_mma's griddep_launch); it then waits (griddep_wait) before reading
+// what that kernel wrote.  Only for a previous kernel whose CTAs are all
+// resident at once, so that none of them waits for an SM this one holds.
 template <int EPI>
-cudaError_t mma_gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st) {
+cudaError_t mma_gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st, bool pdl) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
     GemmArgs ga = base;
     const int row_tiles = (rows + tc::kMR - 1) / tc::kMR;
@@ -1162,17 +1189,19 @@ cudaError_t mma_gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st) {
     cfg.blockDim = dim3(kMT);
     cfg.dynamicSmemBytes = tc::smem_bytes(NM);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1, attr[0].val.clusterDim.y = ga.splits, attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, k_mma<EPI>, ga);
 }
 
 template <int EPI>
-cudaError_t product(bool tensor, const GemmArgs &ga, int rows, int nsm, cudaStream_t st) {
-    return tensor ? mma_gemm<EPI>(ga, rows, nsm, st) : gemm<EPI>(ga, rows, nsm, st);
+cudaError_t product(bool tensor, const GemmArgs &ga, int rows, int nsm, cudaStream_t st, bool pdl = false) {
+    return tensor ? mma_gemm<EPI>(ga, rows, nsm, st, pdl) : gemm<EPI>(ga, rows, nsm, st);
 }
 
 }  // namespace
@@ -1226,10 +1255,13 @@ cudaError_t launch_layer_mm(const DevModel *dm, const DevModel &hd, const Shapes
         ga.x = hd.h;
     }
     ga.nb = E / 32, ga.a = mats({&L.q, &L.k, &L.v});
-    cudaError_t e = product<EPI_QKV>(tensor, ga, L.q.rows + L.k.rows + L.v.rows, nsm, st);
+    // (with the tensor-core products, QKV, attention, gate/up and down start as programmatic dependents of
+    // the kernel before them: products whose CTAs are all resident at once; attention runs several waves,
+    // so the output product after it starts normally)
+    cudaError_t e = product<EPI_QKV>(tensor, ga, L.q.rows + L.k.rows + L.v.rows, nsm, st, tensor);
     ga.norm_w = nullptr;
     // attention (per token, per head and chunk of 64 positions)
-    launch_attention(dm, s, l, m, st, tb);
+    if (e == cudaSuccess) e = launch_attention(dm, s, l, m, st, tb, tensor);
     // x += Wo att
     ga.x = hd.att, ga.nb = E / 32, ga.a = mats({&L.o}), ga.out = hd.x, ga.out_ld = E, ga.ssq_out = tensor;
     if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.o.rows, nsm, st);
@@ -1241,11 +1273,11 @@ cudaError_t launch_layer_mm(const DevModel *dm, const DevModel &hd, const Shapes
         ga.x = hd.h;
     }
     ga.nb = E / 32, ga.a = mats({&L.gate}), ga.b = mats({&L.up}), ga.out = hd.act, ga.out_ld = F;
-    if (e == cudaSuccess) e = product<EPI_SWIGLU>(tensor, ga, L.gate.rows, nsm, st);
+    if (e == cudaSuccess) e = product<EPI_SWIGLU>(tensor, ga, L.gate.rows, nsm, st, tensor);
     ga.norm_w = nullptr;
     // x += Wdown act
     ga.x = hd.act, ga.nb = F / 32, ga.a = mats({&L.down}), ga.b = MatSet{}, ga.out = hd.x, ga.out_ld = E;
-    if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.down.rows, nsm, st);
+    if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.down.rows, nsm, st, tensor);
     return e;
 }
 

@@ -542,6 +542,8 @@ __global__ void __launch_bounds__(kThreads) k_qkv(const DevModel *__restrict__ d
 
 __global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ dmp, int l, const TokBatch *tb) {
     extern __shared__ float smem[];
+    // launched as a programmatic dependent of the QKV product: wait for its q and K/V rows (a no-op otherwise)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const DevModel &dm = *dmp;
     const int t = blockIdx.y;
     const int n = (tb ? tb->pos[t] : dm.state[0] + t) + 1;
@@ -703,8 +705,19 @@ void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaSt
     k_head<<<s.head_ctas, kThreads, smem_bytes(s), st>>>(dm, t_src, adv);
 }
 
-void launch_attention(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb) {
-    k_attn<<<dim3(s.kv_heads * s.nchunk, m), kThreads, smem_bytes(s), st>>>(dm, l, tb);
+cudaError_t launch_attention(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb,
+                             bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(s.kv_heads * s.nchunk, m);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes(s);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_attn, dm, l, tb);
 }
 
 void launch_head_batch(const DevModel *dm, const Shapes &s, TokBatch *tb, int rows, cudaStream_t st) {

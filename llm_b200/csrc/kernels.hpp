@@ -56,7 +56,9 @@ void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_
 void launch_head(const DevModel *dm, const Shapes &s, int t_src, int adv, cudaStream_t st);
 
 // The attention of one layer alone (the m-token path's products are in gemm.cu).
-void launch_attention(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb);
+// pdl: launched as a programmatic dependent of the kernel before it (k_attn waits for it first)
+cudaError_t launch_attention(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb,
+                             bool pdl = false);
 
 // One layer for m <= 64 tokens through the chunked products of gemm.cu
 // (norm, QKV product with bias/RoPE/KV append, attention, output product +
