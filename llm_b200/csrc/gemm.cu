@@ -1174,10 +1174,11 @@ int mma_splits(int epi, int row_tiles, int nb) {
 }
 
 // pdl: launched as a programmatic dependent of the previous kernel in the
-// stream, which lets it in once all of that kernel's CTAs have finished their
-// MMAs (k_mma's griddep_launch); it then waits (griddep_wait) before reading
-// what that kernel wrote.  Only for a previous kernel whose CTAs are all
-// resident at once, so that none of them waits for an SM this one holds.
+// stream, which lets it in once every CTA of that kernel has signalled
+// (k_mma after its MMAs, k_attn at its start) or exited; it then waits
+// (griddep_wait) before reading what that kernel wrote.  Since a CTA signals
+// only once it runs, no CTA of the previous kernel can be left waiting for an
+// SM that this one holds.
 template <int EPI>
 cudaError_t mma_gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st, bool pdl) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
@@ -1255,16 +1256,15 @@ cudaError_t launch_layer_mm(const DevModel *dm, const DevModel &hd, const Shapes
         ga.x = hd.h;
     }
     ga.nb = E / 32, ga.a = mats({&L.q, &L.k, &L.v});
-    // (with the tensor-core products, QKV, attention, gate/up and down start as programmatic dependents of
-    // the kernel before them: products whose CTAs are all resident at once; attention runs several waves,
-    // so the output product after it starts normally)
+    // (with the tensor-core products, every launch of the layer starts as a programmatic dependent of the
+    // kernel before it, which lets it in once all of its CTAs have started or finished their main work)
     cudaError_t e = product<EPI_QKV>(tensor, ga, L.q.rows + L.k.rows + L.v.rows, nsm, st, tensor);
     ga.norm_w = nullptr;
     // attention (per token, per head and chunk of 64 positions)
     if (e == cudaSuccess) e = launch_attention(dm, s, l, m, st, tb, tensor);
     // x += Wo att
     ga.x = hd.att, ga.nb = E / 32, ga.a = mats({&L.o}), ga.out = hd.x, ga.out_ld = E, ga.ssq_out = tensor;
-    if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.o.rows, nsm, st);
+    if (e == cudaSuccess) e = product<EPI_RESID>(tensor, ga, L.o.rows, nsm, st, tensor);
     // act = SwiGLU(Wgate h, Wup h)
     if (tensor) {
         ga.x = hd.x, ga.norm_w = L.ffn_norm;

@@ -542,8 +542,10 @@ __global__ void __launch_bounds__(kThreads) k_qkv(const DevModel *__restrict__ d
 
 __global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ dmp, int l, const TokBatch *tb) {
     extern __shared__ float smem[];
-    // launched as a programmatic dependent of the QKV product: wait for its q and K/V rows (a no-op otherwise)
+    // launched as a programmatic dependent of the QKV product: wait for its q and K/V rows (a no-op otherwise);
+    // then let the output product start its set-up as this grid's last CTAs run
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const DevModel &dm = *dmp;
     const int t = blockIdx.y;
     const int n = (tb ? tb->pos[t] : dm.state[0] + t) + 1;
