@@ -157,7 +157,7 @@ struct GemmArgs {
     const float *x;      // [m][K]
     int m, nb;           // tokens, 32-column blocks of K
     MatSet a, b;         // b: the up matrix of SwiGLU (a: gate)
-    int splits;          // the cluster's CTAs along K (1, 2, 4 or 8)
+    int splits;          // the cluster's CTAs along K (1, 2, 4 or 8; 16 for the tensor-core products)
     int l;               // layer (QKV: which KV cache)
     float *out;          // RESID: x [m][E]; SWIGLU: act [m][F]
     int out_ld;
@@ -858,6 +858,7 @@ __device__ __forceinline__ float epi_out(const EpiIn &e, const float (&v)[NM][4]
 // and commits them to `empty`, which releases the stage.  No block-wide
 // barrier separates K blocks, so staging overlaps the tensor cores.
 constexpr int kMT = kGT + 32;  // threads of k_mma: 8 staging warps and the MMA warp
+constexpr int kMaxSplit = 16;  // CTAs of a cluster along K
 
 template <int EPI>
 __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs ga) {
@@ -1093,24 +1094,29 @@ __global__ void __launch_bounds__(kMT, 1) k_mma(const __grid_constant__ GemmArgs
             const EpiIn e = it == i0 + (int)threadIdx.x ? pre : epi_in<EPI>(ga, dm, g, t, total);
             float sq = 0.f;
             if (g < total) {
-                // every rank's float4 of rows 4u..4u+3 at token t loaded first, then summed in rank order
-                float4 pv[8][NM];
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    if (r < S) {
-                        const float *rs = S > 1 ? cl.map_shared_rank(part, r) : part;
-#pragma unroll
-                        for (int j = 0; j < NM; ++j)
-                            pv[r][j] = *reinterpret_cast<const float4 *>(rs + ((size_t)j * kMN + t) * kPartLd + 4 * u);
-                    }
-                }
+                // the ranks' float4s of rows 4u..4u+3 at token t, loaded 8 ranks at a time, summed in rank order
                 float v[NM][4];
 #pragma unroll
-                for (int j = 0; j < NM; ++j) {
-                    v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
+                for (int j = 0; j < NM; ++j) v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
 #pragma unroll
-                    for (int r = 0; r < 8; ++r)
-                        if (r < S) v[j][0] += pv[r][j].x, v[j][1] += pv[r][j].y, v[j][2] += pv[r][j].z, v[j][3] += pv[r][j].w;
+                for (int r0 = 0; r0 < kMaxSplit; r0 += 8) {
+                    if (r0 >= S) break;
+                    float4 pv[8][NM];
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) {
+                        if (r0 + r < S) {
+                            const float *rs = S > 1 ? cl.map_shared_rank(part, r0 + r) : part;
+#pragma unroll
+                            for (int j = 0; j < NM; ++j)
+                                pv[r][j] = *reinterpret_cast<const float4 *>(rs + ((size_t)j * kMN + t) * kPartLd + 4 * u);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < NM; ++j)
+#pragma unroll
+                        for (int r = 0; r < 8; ++r)
+                            if (r0 + r < S)
+                                v[j][0] += pv[r][j].x, v[j][1] += pv[r][j].y, v[j][2] += pv[r][j].z, v[j][3] += pv[r][j].w;
                 }
                 sq = epi_out<EPI, NM>(e, v);
             }
@@ -1160,15 +1166,16 @@ cudaError_t gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st) {
 // are resident at once, by device (cudaOccupancyMaxActiveClusters: one CTA
 // per SM, and a cluster's CTAs in one GPC), measured by prepare_products.
 constexpr int kMaxDevices = 64;
-int g_mma_clusters[kMaxDevices][4][4];
+int g_mma_clusters[kMaxDevices][4][5];
 
-// CTAs along K per row tile for the tensor-core products: the largest of 8,
-// 4, 2 whose clusters are all resident at once (a second wave would double
-// the time) and that gives each CTA at least 2 K blocks.
+// CTAs along K per row tile for the tensor-core products: the largest of 16,
+// 8, 4, 2 whose clusters are all resident at once (a second wave would double
+// the time) and that gives each CTA at least 2 K blocks.  (16 is a
+// non-portable cluster size: each GPC holds one such cluster at most.)
 int mma_splits(int epi, int row_tiles, int nb) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
-    for (int s = 8, ix = 3; s > 1; s /= 2, --ix)
+    for (int s = kMaxSplit, ix = 4; s > 1; s /= 2, --ix)
         if (nb >= 2 * s && row_tiles <= g_mma_clusters[dev][epi][ix]) return s;
     return 1;
 }
@@ -1213,7 +1220,8 @@ cudaError_t prepare_products() {
                                                {(const void *)k_mma<EPI_SWIGLU>, tc::smem_bytes(2)},
                                                {(const void *)k_mma<EPI_ARGMAX>, tc::smem_bytes(1)}};
     for (const auto &f : fs) {
-        const cudaError_t e = cudaFuncSetAttribute(f.first, cudaFuncAttributeMaxDynamicSharedMemorySize, f.second);
+        cudaError_t e = cudaFuncSetAttribute(f.first, cudaFuncAttributeMaxDynamicSharedMemorySize, f.second);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(f.first, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
     }
     int dev = 0;
@@ -1223,7 +1231,7 @@ cudaError_t prepare_products() {
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
     for (int k = 0; k < 4; ++k)
-        for (int ix = 0; ix < 4; ++ix) {
+        for (int ix = 0; ix < 5; ++ix) {
             const int s = 1 << ix;
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(1, s);
@@ -1236,7 +1244,11 @@ cudaError_t prepare_products() {
             cfg.numAttrs = 1;
             int n = 0;
             e = cudaOccupancyMaxActiveClusters(&n, fs[k].first, &cfg);
-            if (e != cudaSuccess) return e;
+            if (e != cudaSuccess) {
+                if (s <= 8) return e;
+                cudaGetLastError();  // a device without clusters of 16: that split is not used
+                n = 0;
+            }
             g_mma_clusters[dev][k][ix] = n;
         }
     return cudaSuccess;
