@@ -157,7 +157,7 @@ struct GemmArgs {
     const float *x;      // [m][K]
     int m, nb;           // tokens, 32-column blocks of K
     MatSet a, b;         // b: the up matrix of SwiGLU (a: gate)
-    int splits;          // the cluster's CTAs along K (1, 2, 4 or 8; 16 for the tensor-core products)
+    int splits;          // the cluster's CTAs along K (1, 2, 4 or 8; 1-16 for the tensor-core products)
     int l;               // layer (QKV: which KV cache)
     float *out;          // RESID: x [m][E]; SWIGLU: act [m][F]
     int out_ld;
@@ -1162,30 +1162,28 @@ cudaError_t gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, k_gemm<EPI>, ga);
 }
 
-// Clusters of s CTAs (s = 1, 2, 4, 8) of each tensor-core product kernel that
-// are resident at once, by device (cudaOccupancyMaxActiveClusters: one CTA
-// per SM, and a cluster's CTAs in one GPC), measured by prepare_products.
+// Clusters of s CTAs (s = 1..16) of each tensor-core product kernel that are
+// resident at once, by device (cudaOccupancyMaxActiveClusters: one CTA per
+// SM, and a cluster's CTAs in one GPC), measured by prepare_products.
 constexpr int kMaxDevices = 64;
-int g_mma_clusters[kMaxDevices][4][5];
+int g_mma_clusters[kMaxDevices][4][kMaxSplit + 1];
 
-// CTAs along K per row tile for the tensor-core products: the largest of 16,
-// 8, 4, 2 whose clusters are all resident at once (a second wave would double
-// the time) and that gives each CTA at least 2 K blocks.  (16 is a
-// non-portable cluster size: each GPC holds one such cluster at most.)
+// CTAs along K per row tile for the tensor-core products.  Every cluster must
+// be resident at once (a second wave would double the time) and each CTA
+// must get at least 2 K blocks; among those splits, the one whose CTAs take
+// the fewest K blocks at most (the cluster waits for its slowest CTA), and
+// of equals the smallest (less to reduce).  Sizes above 8 are non-portable:
+// a GPC holds one such cluster at most.
 int mma_splits(int epi, int row_tiles, int nb) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
-    for (int s = kMaxSplit, ix = 4; s > 1; s /= 2, --ix)
-        if (nb >= 2 * s && row_tiles <= g_mma_clusters[dev][epi][ix]) return s;
-    return 1;
+    int best = 1, most = nb;
+    for (int s = 2; s <= kMaxSplit; ++s)
+        if (nb >= 2 * s && row_tiles <= g_mma_clusters[dev][epi][s] && (nb + s - 1) / s < most)
+            best = s, most = (nb + s - 1) / s;
+    return best;
 }
 
-// pdl: launched as a programmatic dependent of the previous kernel in the
-// stream, which lets it in once every CTA of that kernel has signalled
-// (k_mma after its MMAs, k_attn at its start) or exited; it then waits
-// (griddep_wait) before reading what that kernel wrote.  Since a CTA signals
-// only once it runs, no CTA of the previous kernel can be left waiting for an
-// SM that this one holds.
 template <int EPI>
 cudaError_t mma_gemm(const GemmArgs &base, int rows, int nsm, cudaStream_t st, bool pdl) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
@@ -1231,8 +1229,7 @@ cudaError_t prepare_products() {
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
     for (int k = 0; k < 4; ++k)
-        for (int ix = 0; ix < 5; ++ix) {
-            const int s = 1 << ix;
+        for (int s = 1; s <= kMaxSplit; ++s) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(1, s);
             cfg.blockDim = dim3(kMT);
@@ -1249,7 +1246,7 @@ cudaError_t prepare_products() {
                 cudaGetLastError();  // a device without clusters of 16: that split is not used
                 n = 0;
             }
-            g_mma_clusters[dev][k][ix] = n;
+            g_mma_clusters[dev][k][s] = n;
         }
     return cudaSuccess;
 }
