@@ -44,6 +44,13 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// 16 bytes global -> shared, asynchronously (both 16-byte aligned); completed by cp.async.wait_all.
+__device__ __forceinline__ void cp_async16(float *dst, const float *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src)
+                 : "memory");
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
@@ -295,14 +302,16 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
     __shared__ int last;
     const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
     const int nd4 = HD / 4;
+    // the chunk's K and V rows and the group's queries by asynchronous 16-byte copies, all in flight at once
     for (int i = threadIdx.x; i < cnt * nd4; i += kThreads) {
         const int p = i / nd4, d4 = i % nd4;
         const size_t row = (size_t)(p0 + p) * dm.kvd + g * HD;
-        *reinterpret_cast<float4 *>(ks + p * KS + d4 * 4) = __ldcg(reinterpret_cast<const float4 *>(kv + row) + d4);
-        *reinterpret_cast<float4 *>(vs + p * KS + d4 * 4) =
-            __ldcg(reinterpret_cast<const float4 *>(kv + (size_t)dm.ctx * dm.kvd + row) + d4);
+        cp_async16(ks + p * KS + d4 * 4, kv + row + 4 * d4);
+        cp_async16(vs + p * KS + d4 * 4, kv + (size_t)dm.ctx * dm.kvd + row + 4 * d4);
     }
-    for (int i = threadIdx.x; i < grp * HD; i += kThreads) qg[i] = __ldcg(dm.q + (size_t)t * dm.embd + g * grp * HD + i);
+    for (int i = threadIdx.x; i < grp * nd4; i += kThreads)
+        cp_async16(qg + 4 * i, dm.q + (size_t)t * dm.embd + g * grp * HD + 4 * i);
+    asm volatile("cp.async.commit_group;\n cp.async.wait_all;" ::: "memory");
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int j = warp; j < grp; j += kWarps) {
