@@ -4,22 +4,28 @@
 //
 // The reference runs a prefill chunk as its fused q4 kernels over a z axis of
 // tokens (fused.go:294-320, kernels_fused.go:28-73): every token re-reads the
-// weights.  Here a CTA owns a tile of 64 tokens x 64 weight rows, stages one
-// 32-column block of the activations and of the dequantised weights in
-// shared memory per step, and each thread accumulates a 4 x 4 register tile,
-// so a weight block is read once for all tokens of the chunk.  Weights are
-// dequantised exactly (f16 scale times a small integer is exact in f32); the
-// products are f32 FMAs, summed per block and then over blocks (cpu.go:143-222
-// sums a block, then d * block over blocks).
+// weights.  Here a weight block is read once for all tokens of the chunk, in
+// one of two kernels:
 //
-// Few row tiles (e.g. 9 for a 576-row output) would leave most SMs idle, so
-// the K range is split over the CTAs of a thread-block cluster (up to 8);
-// each keeps its partial tile in shared memory, and after a cluster barrier
-// each CTA adds the cluster's partials for its share of the tokens through
-// distributed shared memory, in rank order (deterministic), and runs the
-// epilogue: QKV bias + RoPE + q store + KV append, the residual add,
-// SwiGLU, or per-token argmax partials for the vocabulary head.  The next
-// K block's loads are issued before the current block's products.
+//   k_mma (the default): the tensor cores.  A CTA owns 128 weight rows x 64
+//   tokens; each 32-column block of the weights (dequantised exactly in f32)
+//   and of the activations is split exactly into bf16 pieces, and the piece
+//   products that reach 2^-18 of a x run as tcgen05.mma with f32
+//   accumulators in tensor memory.
+//
+//   k_gemm (an A/B path): the FP32 CUDA cores.  A CTA owns 64 tokens x 64
+//   weight rows and each thread accumulates a 4 x 4 register tile of f32
+//   FMAs, summed per block and then over blocks (cpu.go:143-222 sums a block,
+//   then d * block over blocks).
+//
+// Few row tiles (e.g. 5 for a 576-row output) would leave most SMs idle, so
+// the K range is split over the CTAs of a thread-block cluster (up to 8 for
+// k_gemm, 16 for k_mma); each keeps its partial tile in shared memory, and
+// after a cluster barrier each CTA adds the cluster's partials for its share
+// of the tokens through distributed shared memory, in rank order
+// (deterministic), and runs the epilogue: QKV bias + RoPE + q store + KV
+// append, the residual add, SwiGLU, or per-token argmax partials for the
+// vocabulary head.
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
