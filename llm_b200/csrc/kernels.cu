@@ -372,19 +372,55 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // per head j: the chunks' weights f[j][c] = exp(max_c - M) (double) and the sum of f * l in chunk order,
+    // computed once in the K/V rows' shared memory (free now); then each (head, dimension) folds the chunks'
+    // partial sums in chunk order with 8 chunks' loads in flight.  (Up to 2 chunks, or a context whose
+    // weights do not fit, each thread computes the weights itself.)
+    double *fw = reinterpret_cast<double *>(sm.vec), *lt = fw + (size_t)grp * nch;
+    const bool fit = nch > 2 && (size_t)grp * (nch + 1) * sizeof(double) <= (size_t)2 * kAttnChunk * KS * sizeof(float);
+    if (fit) {
+        for (int j = warp; j < grp; j += kWarps) {
+            const size_t th = (size_t)t * dm.heads + g * grp + j;
+            float M = -FLT_MAX;
+            for (int cc = lane; cc < nch; cc += 32) M = fmaxf(M, __ldcg(&dm.part_ml[th * dm.nchunk + cc].x));
+            M = warp_max(M);
+            for (int cc = lane; cc < nch; cc += 32)
+                fw[j * nch + cc] = exp((double)__ldcg(&dm.part_ml[th * dm.nchunk + cc].x) - (double)M);
+            __syncwarp();
+            if (lane == 0) {
+                double l = 0.0;
+                for (int cc = 0; cc < nch; ++cc) l = fma(fw[j * nch + cc], (double)__ldcg(&dm.part_ml[th * dm.nchunk + cc].y), l);
+                lt[j] = l;
+            }
+        }
+        __syncthreads();
+    }
     for (int i = threadIdx.x; i < grp * HD; i += kThreads) {
         const int j = i / HD, d = i % HD, h = g * grp + j;
         const size_t th = (size_t)t * dm.heads + h;
-        float M = -FLT_MAX;
-        for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(&dm.part_ml[th * dm.nchunk + cc].x));
-        double lt = 0.0, ot = 0.0;
-        for (int cc = 0; cc < nch; ++cc) {
-            const float2 ml = __ldcg(&dm.part_ml[th * dm.nchunk + cc]);
-            const double f = exp((double)ml.x - (double)M);
-            lt = fma(f, (double)ml.y, lt);
-            ot = fma(f, (double)__ldcg(dm.part_pv + (th * dm.nchunk + cc) * HD + d), ot);
+        const float *pv = dm.part_pv + th * dm.nchunk * HD + d;
+        double ot = 0.0, l = 0.0;
+        if (fit) {
+            for (int c0 = 0; c0 < nch; c0 += 8) {
+                float v8[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v8[k] = c0 + k < nch ? __ldcg(pv + (size_t)(c0 + k) * HD) : 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (c0 + k < nch) ot = fma(fw[j * nch + c0 + k], (double)v8[k], ot);
+            }
+            l = lt[j];
+        } else {
+            float M = -FLT_MAX;
+            for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, __ldcg(&dm.part_ml[th * dm.nchunk + cc].x));
+            for (int cc = 0; cc < nch; ++cc) {
+                const float2 ml = __ldcg(&dm.part_ml[th * dm.nchunk + cc]);
+                const double f = exp((double)ml.x - (double)M);
+                l = fma(f, (double)ml.y, l);
+                ot = fma(f, (double)__ldcg(pv + (size_t)cc * HD), ot);
+            }
         }
-        dm.att[(size_t)t * dm.embd + h * HD + d] = (float)(ot / lt);
+        dm.att[(size_t)t * dm.embd + h * HD + d] = (float)(ot / l);
     }
 }
 
