@@ -470,7 +470,8 @@ Error open_model(Model &m, const ReadAt &read, uint64_t size, int ctx) {
     }
     CUDA_TRY(cudaHostAlloc(&m.h_tokens, (size_t)(ctx + 2 * kMaxDecodeBatch + 1) * 4, cudaHostAllocDefault));
     CUDA_TRY(cudaHostAlloc(&m.h_state, 16, cudaHostAllocDefault));
-    CUDA_TRY(cudaHostAlloc(&m.h_err, 4, cudaHostAllocDefault));
+    CUDA_TRY(cudaHostAlloc(&m.h_err, 4 * 4, cudaHostAllocDefault));  // [0] checks; [1 + slot] a decode launch's
+    std::memset(m.h_err, 0, 4 * 4);
     CUDA_TRY(cudaStreamSynchronize(m.st));
     m.stats.submits++;
     return err;
@@ -484,9 +485,10 @@ cudaError_t reset_tags(Model &m);
 // error it is cleared, and so are the persistent kernel's tagged buffers: a
 // launch that gave up leaves words whose tags the next launch would reuse
 // (the epoch counter advances only when a launch completes).
-Error check_device(Model &m) {
-    CUDA_TRY(cudaMemcpyAsync(m.h_err, m.hdm.err, 4, cudaMemcpyDeviceToHost, m.st));
-    CUDA_TRY(cudaStreamSynchronize(m.st));
+// The device error word, already copied to m.h_err by a synchronised stream: a
+// device error becomes LLMB_ERR_DEVICE, after the word, the tags and the
+// token count of the persistent kernel are reset.
+Error device_status(Model &m) {
     if (*m.h_err != 0) {
         const int e = *m.h_err;
         *m.h_err = 0;
@@ -502,6 +504,12 @@ Error check_device(Model &m) {
         return {LLMB_ERR_DEVICE, std::string("llm: ") + what};
     }
     return {LLMB_OK, ""};
+}
+
+Error check_device(Model &m) {
+    CUDA_TRY(cudaMemcpyAsync(m.h_err, m.hdm.err, 4, cudaMemcpyDeviceToHost, m.st));
+    CUDA_TRY(cudaStreamSynchronize(m.st));
+    return device_status(m);
 }
 
 int layers_to_run(const Model &m) {
@@ -698,6 +706,9 @@ Error generate(Model &m, const int32_t *prompt, int np, int n, int32_t eos, llmb
             CUDA_TRY(cudaEventRecord(m.lev[k & 3][1], m.st));
             CUDA_TRY(cudaMemcpyAsync(slot[sl], m.hdm.tokens + np + issued, (size_t)cnt * 4, cudaMemcpyDeviceToHost,
                                      m.st));
+            // the device error word after this launch, read back with its tokens (no stream-wide wait, so
+            // the other launch stays in flight)
+            CUDA_TRY(cudaMemcpyAsync(m.h_err + 1 + sl, m.hdm.err, 4, cudaMemcpyDeviceToHost, m.st));
             CUDA_TRY(cudaEventRecord(m.lev[k & 3][2], m.st));
             tm.record_ms += now_ms() - ta;
             q[(qh + qn) & 1] = {cnt, sl};
@@ -714,11 +725,15 @@ Error generate(Model &m, const int32_t *prompt, int np, int n, int32_t eos, llmb
         cudaEventElapsedTime(&kms, m.lev[li][0], m.lev[li][1]);
         tm.decode_kernel_ms += kms;
         tm.decode_launches++;
-        if ((err = check_device(m)).code) return err;
+        if (m.h_err[1 + q[qh].slot] != 0) {  // a device error: the full check resets the state and reports it
+            m.h_err[1 + q[qh].slot] = 0;
+            if ((err = check_device(m)).code) return err;
+        }
         pending = q[qh].cnt, pending_slot = q[qh].slot;
         qh = (qh + 1) & 1, qn--;
     }
     CUDA_TRY(cudaStreamSynchronize(m.st));  // launches queued past a stop
+    if ((err = check_device(m)).code) return err;
     CUDA_TRY(cudaEventRecord(m.ev3, m.st));
     CUDA_TRY(cudaEventSynchronize(m.ev3));
     tm.decode_ms = now_ms() - t1;
@@ -781,10 +796,12 @@ Error run_batch(Model &m, int cnt, int nh) {
         m.stats.dispatches += mm ? 3 : 1;
         CUDA_TRY(cudaMemcpyAsync(m.h_tb->out, m.tb->out, (size_t)nh * 4, cudaMemcpyDeviceToHost, m.st));
     }
+    // the error word with the tokens: one synchronisation per batch
+    CUDA_TRY(cudaMemcpyAsync(m.h_err, m.hdm.err, 4, cudaMemcpyDeviceToHost, m.st));
     CUDA_TRY(cudaGetLastError());
     m.stats.submits++;
     CUDA_TRY(cudaStreamSynchronize(m.st));
-    return check_device(m);
+    return device_status(m);
 }
 
 Error generate_batch(Model &m, const int32_t *prompts, const int *lens, int nseq, int n, int32_t eos, int32_t *out,
