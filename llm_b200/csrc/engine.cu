@@ -659,8 +659,9 @@ Error generate(Model &m, const int32_t *prompt, int np, int n, int32_t eos, llmb
     // the first sampled token comes back with the prefill (gpu.go:954-958)
     int32_t *slot[2] = {m.h_tokens, m.h_tokens + kMaxDecodeBatch};
     CUDA_TRY(cudaMemcpyAsync(slot[0], m.hdm.tokens + np, 4, cudaMemcpyDeviceToHost, m.st));
+    CUDA_TRY(cudaMemcpyAsync(m.h_err, m.hdm.err, 4, cudaMemcpyDeviceToHost, m.st));
     CUDA_TRY(cudaStreamSynchronize(m.st));
-    if ((err = check_device(m)).code) return err;
+    if ((err = device_status(m)).code) return err;
     tm.prefill_ms = now_ms() - t0;
     tm.prompt_tokens = np;
     const double t1 = now_ms();
