@@ -290,7 +290,7 @@ __device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bo
 // The last CTA of (token, group) to finish merges the chunks of the group's
 // heads (kernels_fused.go:150-170) into att.  Groups of up to 8 query heads
 // per KV head; more take several rounds of the warps.
-__device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, int item, uint32_t *att_cnt,
+__device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, int hist_end, int item, uint32_t *att_cnt,
                            const Smem &sm) {
     const int HD = dm.head_dim, grp = dm.heads / dm.kv_heads;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
@@ -302,13 +302,23 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
     __shared__ int last;
     const int p0 = c * kAttnChunk, cnt = min(kAttnChunk, n - p0);
     const int nd4 = HD / 4;
-    // the chunk's K and V rows and the group's queries by asynchronous 16-byte copies, all in flight at once
-    for (int i = threadIdx.x; i < cnt * nd4; i += kThreads) {
-        const int p = i / nd4, d4 = i % nd4;
-        const size_t row = (size_t)(p0 + p) * dm.kvd + g * HD;
-        cp_async16(ks + p * KS + d4 * 4, kv + row + 4 * d4);
-        cp_async16(vs + p * KS + d4 * 4, kv + (size_t)dm.ctx * dm.kvd + row + 4 * d4);
-    }
+    // the chunk's K and V rows and the group's queries by asynchronous 16-byte copies, all in flight at once.
+    // Rows below hist_end were written by earlier launches, so their copies start before the wait for the
+    // QKV product (a programmatic dependency: it writes this launch's rows and the queries); the rest after.
+    const int pe = min(cnt, max(0, hist_end - p0));
+    auto copy_rows = [&](int i0, int i1) {
+        for (int i = i0 + (int)threadIdx.x; i < i1; i += kThreads) {
+            const int p = i / nd4, d4 = i % nd4;
+            const size_t row = (size_t)(p0 + p) * dm.kvd + g * HD;
+            cp_async16(ks + p * KS + d4 * 4, kv + row + 4 * d4);
+            cp_async16(vs + p * KS + d4 * 4, kv + (size_t)dm.ctx * dm.kvd + row + 4 * d4);
+        }
+    };
+    copy_rows(0, pe * nd4);
+    // then let the output product start its set-up as this grid's last CTAs run
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    copy_rows(pe * nd4, cnt * nd4);
     for (int i = threadIdx.x; i < grp * nd4; i += kThreads)
         cp_async16(qg + 4 * i, dm.q + (size_t)t * dm.embd + g * grp * HD + 4 * i);
     asm volatile("cp.async.commit_group;\n cp.async.wait_all;" ::: "memory");
@@ -587,16 +597,29 @@ __global__ void __launch_bounds__(kThreads) k_qkv(const DevModel *__restrict__ d
 
 __global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ dmp, int l, const TokBatch *tb) {
     extern __shared__ float smem[];
-    // launched as a programmatic dependent of the QKV product: wait for its q and K/V rows (a no-op otherwise);
-    // then let the output product start its set-up as this grid's last CTAs run
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Launched as a programmatic dependent of the QKV product, which writes the queries and this launch's K/V
+    // rows; phase_attn waits for it (a no-op otherwise) after requesting the rows written before it.  The
+    // positions and KV slots were written before the launch.
     const DevModel &dm = *dmp;
     const int t = blockIdx.y;
     const int n = (tb ? tb->pos[t] : dm.state[0] + t) + 1;
     const int nch = (n + kAttnChunk - 1) / kAttnChunk;
     if ((int)blockIdx.x >= dm.kv_heads * nch) return;
-    phase_attn(dm, kv_of(dm, tb, l, t), t, n, blockIdx.x, dm.att_cnt, smem_views(smem, dm));
+    // hist_end: the first position of token t's sequence that this launch writes (its lowest position among
+    // the batch's tokens of the same KV slot; for one sequence, the chunk's first position)
+    __shared__ int hist_end;
+    if (threadIdx.x < 32) {
+        int h = tb ? n - 1 : dm.state[0];
+        if (tb) {
+            const int slot = tb->slot[t];
+            for (int u = threadIdx.x; u < (int)gridDim.y; u += 32)
+                if (tb->slot[u] == slot) h = min(h, tb->pos[u]);
+            for (int o = 16; o; o >>= 1) h = min(h, __shfl_xor_sync(kFull, h, o));
+        }
+        if (threadIdx.x == 0) hist_end = h;
+    }
+    __syncthreads();
+    phase_attn(dm, kv_of(dm, tb, l, t), t, n, hist_end, blockIdx.x, dm.att_cnt, smem_views(smem, dm));
 }
 
 __global__ void __launch_bounds__(kThreads) k_oproj(const DevModel *__restrict__ dmp, int l) {
