@@ -388,22 +388,59 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
     // weights do not fit, each thread computes the weights itself.)
     double *fw = reinterpret_cast<double *>(sm.vec), *lt = fw + (size_t)grp * nch;
     const bool fit = nch > 2 && (size_t)grp * (nch + 1) * sizeof(double) <= (size_t)2 * kAttnChunk * KS * sizeof(float);
+    // one (head, dimension) per thread: its first kPre chunks' partial sums are requested before the weights
+    // are computed, so that the two rounds of loads overlap
+    constexpr int kPre = 4;
+    const bool one = fit && grp * HD <= kThreads;
+    float pre[kPre];
+    if (one && (int)threadIdx.x < grp * HD) {
+        const int j = threadIdx.x / HD, d = threadIdx.x % HD;
+        const float *pv = dm.part_pv + ((size_t)t * dm.heads + g * grp + j) * dm.nchunk * HD + d;
+#pragma unroll
+        for (int k = 0; k < kPre; ++k) pre[k] = k < nch ? __ldcg(pv + (size_t)k * HD) : 0.f;
+    }
     if (fit) {
         for (int j = warp; j < grp; j += kWarps) {
             const size_t th = (size_t)t * dm.heads + g * grp + j;
             float M = -FLT_MAX;
-            for (int cc = lane; cc < nch; cc += 32) M = fmaxf(M, __ldcg(&dm.part_ml[th * dm.nchunk + cc].x));
+            float2 ml0 = make_float2(-FLT_MAX, 0.f);  // this lane's first chunk (most contexts have at most 32)
+            if (lane < nch) ml0 = __ldcg(&dm.part_ml[th * dm.nchunk + lane]);
+            M = ml0.x;
+            for (int cc = lane + 32; cc < nch; cc += 32) M = fmaxf(M, __ldcg(&dm.part_ml[th * dm.nchunk + cc].x));
             M = warp_max(M);
-            for (int cc = lane; cc < nch; cc += 32)
-                fw[j * nch + cc] = exp((double)__ldcg(&dm.part_ml[th * dm.nchunk + cc].x) - (double)M);
-            __syncwarp();
-            if (lane == 0) {
-                double l = 0.0;
-                for (int cc = 0; cc < nch; ++cc) l = fma(fw[j * nch + cc], (double)__ldcg(&dm.part_ml[th * dm.nchunk + cc].y), l);
-                lt[j] = l;
+            // the weights and the sum of f * l over the chunks (lanes, then a fixed shuffle tree)
+            double l = 0.0;
+            for (int cc = lane; cc < nch; cc += 32) {
+                const float2 ml = cc == lane ? ml0 : __ldcg(&dm.part_ml[th * dm.nchunk + cc]);
+                const double f = exp((double)ml.x - (double)M);
+                fw[j * nch + cc] = f;
+                l = fma(f, (double)ml.y, l);
             }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(kFull, l, o);
+            if (lane == 0) lt[j] = l;
         }
         __syncthreads();
+    }
+    if (one) {
+        if ((int)threadIdx.x < grp * HD) {
+            const int j = threadIdx.x / HD, d = threadIdx.x % HD, h = g * grp + j;
+            const float *pv = dm.part_pv + ((size_t)t * dm.heads + h) * dm.nchunk * HD + d;
+            double ot = 0.0;
+#pragma unroll
+            for (int k = 0; k < kPre; ++k)
+                if (k < nch) ot = fma(fw[j * nch + k], (double)pre[k], ot);
+            for (int c0 = kPre; c0 < nch; c0 += 8) {  // the rest, 8 chunks' loads in flight
+                float v8[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v8[k] = c0 + k < nch ? __ldcg(pv + (size_t)(c0 + k) * HD) : 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (c0 + k < nch) ot = fma(fw[j * nch + c0 + k], (double)v8[k], ot);
+            }
+            dm.att[(size_t)t * dm.embd + h * HD + d] = (float)(ot / lt[j]);
+        }
+        return;
     }
     for (int i = threadIdx.x; i < grp * HD; i += kThreads) {
         const int j = i / HD, d = i % HD, h = g * grp + j;
