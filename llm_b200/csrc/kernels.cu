@@ -290,6 +290,7 @@ __device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bo
 // The last CTA of (token, group) to finish merges the chunks of the group's
 // heads (kernels_fused.go:150-170) into att.  Groups of up to 8 query heads
 // per KV head; more take several rounds of the warps.
+template <bool kDirect>
 __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, int hist_end, int item, uint32_t *att_cnt,
                            const Smem &sm) {
     const int HD = dm.head_dim, grp = dm.heads / dm.kv_heads;
@@ -365,11 +366,24 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
             }
         }
         const size_t th = (size_t)t * dm.heads + h;
-        float *pv = dm.part_pv + (th * dm.nchunk + c) * HD + 2 * lane;
-        pv[0] = o0, pv[1] = o1;
-        if (two) pv[64] = o2, pv[65] = o3;
-        if (lane == 0) dm.part_ml[th * dm.nchunk + c] = make_float2(mx, lsum);
+        if constexpr (kDirect) {
+            // the whole context in one chunk: o / l straight into att (by the reciprocal: within 1.5 ulp of
+            // the merge's correctly rounded quotient), with no partials and no merge; else the partials
+            const bool direct = nch == 1;
+            const float r = direct ? __frcp_rn(lsum) : 1.f;
+            float *dst = direct ? dm.att + (size_t)t * dm.embd + h * HD + 2 * lane
+                                : dm.part_pv + (th * dm.nchunk + c) * HD + 2 * lane;
+            dst[0] = __fmul_rn(o0, r), dst[1] = __fmul_rn(o1, r);
+            if (two) dst[64] = __fmul_rn(o2, r), dst[65] = __fmul_rn(o3, r);
+            if (!direct && lane == 0) dm.part_ml[th * dm.nchunk + c] = make_float2(mx, lsum);
+        } else {
+            float *pv = dm.part_pv + (th * dm.nchunk + c) * HD + 2 * lane;
+            pv[0] = o0, pv[1] = o1;
+            if (two) pv[64] = o2, pv[65] = o3;
+            if (lane == 0) dm.part_ml[th * dm.nchunk + c] = make_float2(mx, lsum);
+        }
     }
+    if (kDirect && nch == 1) return;  // no partials, no merge
     // the last arriving CTA of this (token, group) merges the group's heads
     __syncthreads();
     const size_t tg = (size_t)t * dm.kv_heads + g;
@@ -632,6 +646,9 @@ __global__ void __launch_bounds__(kThreads) k_qkv(const DevModel *__restrict__ d
     phase_qkv(dm, l, t, pos, tok, l == 0, kv_of(dm, tb, l, t), blockIdx.x, gridDim.x, smem_views(smem, dm));
 }
 
+// kDirect: a token whose context fits one chunk writes its output without partials or a merge (single-sequence
+// chunks; measured slower for the multi-stream batches, which take k_attn<false>).
+template <bool kDirect>
 __global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ dmp, int l, const TokBatch *tb) {
     extern __shared__ float smem[];
     // Launched as a programmatic dependent of the QKV product, which writes the queries and this launch's K/V
@@ -656,7 +673,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(const DevModel *__restrict__ 
         if (threadIdx.x == 0) hist_end = h;
     }
     __syncthreads();
-    phase_attn(dm, kv_of(dm, tb, l, t), t, n, hist_end, blockIdx.x, dm.att_cnt, smem_views(smem, dm));
+    phase_attn<kDirect>(dm, kv_of(dm, tb, l, t), t, n, hist_end, blockIdx.x, dm.att_cnt, smem_views(smem, dm));
 }
 
 __global__ void __launch_bounds__(kThreads) k_oproj(const DevModel *__restrict__ dmp, int l) {
@@ -781,8 +798,9 @@ cudaError_t prepare_kernels(const Shapes &s) {
     if (sh == set) return cudaSuccess;
     set = sh;
     cudaError_t e = cudaSuccess;
-    for (const void *k : {(const void *)k_qkv, (const void *)k_attn, (const void *)k_oproj, (const void *)k_gateup,
-                          (const void *)k_down, (const void *)k_head, (const void *)k_head_batch})
+    for (const void *k : {(const void *)k_qkv, (const void *)k_attn<true>, (const void *)k_attn<false>,
+                          (const void *)k_oproj, (const void *)k_gateup, (const void *)k_down, (const void *)k_head,
+                          (const void *)k_head_batch})
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sh);
     return e;
 }
@@ -802,7 +820,8 @@ static inline unsigned ctas_for(int tiles) { return (unsigned)((tiles + kWarps -
 void launch_layer(const DevModel *dm, const Shapes &s, int l, int m, cudaStream_t st, const TokBatch *tb) {
     const size_t sh = smem_bytes(s);
     k_qkv<<<dim3(ctas_for(s.qkv_tiles), m), kThreads, sh, st>>>(dm, l, tb);
-    k_attn<<<dim3(s.kv_heads * s.nchunk, m), kThreads, sh, st>>>(dm, l, tb);
+    if (tb) k_attn<false><<<dim3(s.kv_heads * s.nchunk, m), kThreads, sh, st>>>(dm, l, tb);
+    else k_attn<true><<<dim3(s.kv_heads * s.nchunk, m), kThreads, sh, st>>>(dm, l, tb);
     k_oproj<<<dim3(ctas_for(s.o_tiles), m), kThreads, sh, st>>>(dm, l);
     k_gateup<<<dim3(ctas_for(s.gu_tiles), m), kThreads, sh, st>>>(dm, l);
     k_down<<<dim3(ctas_for(s.down_tiles), m), kThreads, sh, st>>>(dm, l);
@@ -824,7 +843,7 @@ cudaError_t launch_attention(const DevModel *dm, const Shapes &s, int l, int m, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_attn, dm, l, tb);
+    return tb ? cudaLaunchKernelEx(&cfg, k_attn<false>, dm, l, tb) : cudaLaunchKernelEx(&cfg, k_attn<true>, dm, l, tb);
 }
 
 void launch_head_batch(const DevModel *dm, const Shapes &s, TokBatch *tb, int rows, cudaStream_t st) {
