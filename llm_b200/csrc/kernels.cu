@@ -289,7 +289,9 @@ __device__ void phase_qkv(const DevModel &dm, int l, int t, int pos, int tok, bo
 // dimensions 2d, 2d + 1 of the exp-weighted V rows (kernels_fused.go:82-146).
 // The last CTA of (token, group) to finish merges the chunks of the group's
 // heads (kernels_fused.go:150-170) into att.  Groups of up to 8 query heads
-// per KV head; more take several rounds of the warps.
+// per KV head; more take several rounds of the warps.  With kDirect, a token
+// whose n positions fit one chunk writes o / l into att itself, with no
+// partials and no merge.
 template <bool kDirect>
 __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, int hist_end, int item, uint32_t *att_cnt,
                            const Smem &sm) {
@@ -316,7 +318,7 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
         }
     };
     copy_rows(0, pe * nd4);
-    // then let the output product start its set-up as this grid's last CTAs run
+    // wait for the QKV product, then let the output product start its set-up as this grid's last CTAs run
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     copy_rows(pe * nd4, cnt * nd4);
