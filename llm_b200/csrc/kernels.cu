@@ -400,9 +400,8 @@ __device__ void phase_attn(const DevModel &dm, const float *kv, int t, int n, in
     __threadfence();
     // per head j: the chunks' weights f[j][c] = exp(max_c - M) (double) and the sum of f * l (over the lanes,
     // then a fixed shuffle tree), computed once in the K/V rows' shared memory (free now); then each (head,
-    // dimension) folds the chunks'
-    // partial sums in chunk order with 8 chunks' loads in flight.  (Up to 2 chunks, or a context whose
-    // weights do not fit, each thread computes the weights itself.)
+    // dimension) folds the chunks' partial sums in chunk order with 8 chunks' loads in flight.  (Up to 2
+    // chunks, or a context whose weights do not fit, each thread computes the weights itself.)
     double *fw = reinterpret_cast<double *>(sm.vec), *lt = fw + (size_t)grp * nch;
     const bool fit = nch > 2 && (size_t)grp * (nch + 1) * sizeof(double) <= (size_t)2 * kAttnChunk * KS * sizeof(float);
     // one (head, dimension) per thread: its first kPre chunks' partial sums are requested before the weights
